@@ -1,0 +1,306 @@
+"""CUDA codec parity through the C-ABI: bit-exact wire bytes and decoded pages against the oracle and the
+reference's golden vectors, at small sizes, at the benchmark configurations' full sizes, with block tables,
+per-page metadata, misaligned blob strides, tampering and batch failure."""
+from __future__ import annotations
+
+import struct
+
+import numpy as np
+import pytest
+import torch
+
+import helpers
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+
+
+@pytest.fixture(scope="module")
+def ext():
+    from ztcp_b200 import build, fused_ext
+
+    build.build()
+    assert torch.cuda.is_available()
+    return fused_ext
+
+
+def _keys(m):
+    return dict(k0=m["key"][0], k1=m["key"][1], mk0=m["mac_key"][0], mk1=m["mac_key"][1], k2=m["key"][2],
+                k3=m["key"][3])
+
+
+def gpu_encode(ext, k, v, toks, rope, preset, rope_mode, exp, m):
+    k = k.to(DEV)
+    v = None if v is None else v.to(DEV)
+    out = torch.empty((k.shape[0], 48 + exp), dtype=torch.uint8, device=DEV)
+    ext.fused_encode_cold_pages_peak_into_cpu(k, v, torch.as_tensor(toks).to(DEV), out, preset, rope_mode, rope, exp,
+                                              m["tenant"], m["model"], m["layer"], m["head_group"], m["base_seq"],
+                                              **_keys(m))
+    torch.cuda.synchronize()
+    return out
+
+
+def gpu_decode(ext, blobs, toks, shape4, rope, mla, m):
+    k = torch.empty(shape4, dtype=torch.float16, device=DEV)
+    v = None if mla else torch.empty(shape4, dtype=torch.float16, device=DEV)
+    ext.fused_decode_cold_pages_peak_into_cpu(blobs.to(DEV), torch.as_tensor(toks).to(DEV), k, v, rope, mla,
+                                              m["tenant"], m["model"], m["layer"], **_keys(m))
+    return k, v
+
+
+def test_chacha20_kats(ext):
+    for v in helpers.load_json("kat_chacha20.json"):
+        data = torch.tensor(list(bytes.fromhex(v["data"])), dtype=torch.uint8, device=DEV)
+        key = torch.tensor(list(bytes.fromhex(v["key"])), dtype=torch.uint8)
+        nonce = torch.tensor(list(bytes.fromhex(v["nonce"])), dtype=torch.uint8)
+        out = ext.chacha20_rfc8439_xor_cpu(data, key, v["counter"], nonce)
+        assert bytes(out.cpu().numpy()).hex() == v["out"]
+
+
+def test_siphash_kats(ext):
+    for v in helpers.load_json("kat_siphash.json"):
+        k0, k1 = struct.unpack("<QQ", bytes.fromhex(v["key"]))
+        data = torch.tensor(list(bytes.fromhex(v["data"])), dtype=torch.uint8, device=DEV)
+        assert bytes(ext.siphash24_128_cpu(data, k0, k1).cpu().numpy()).hex() == v["tag"]
+
+
+def test_codec_small_golden(ext):
+    cases, arrays = helpers.small_cases()
+    for c in cases:
+        i = c["id"]
+        shape = (-1, c["T"], c["H"], c["D"])
+        k = torch.from_numpy(arrays[f"k{i}"].reshape(shape).view(np.float16).copy())
+        v = None if c["mla"] else torch.from_numpy(arrays[f"v{i}"].reshape(shape).view(np.float16).copy())
+        toks = torch.from_numpy(arrays[f"tok{i}"])
+        blobs = gpu_encode(ext, k, v, toks, c["rope"], c["preset"], c["rope_mode"], c["expected_payload"],
+                           c["material"])
+        np.testing.assert_array_equal(blobs.cpu().numpy(), arrays[f"blobs{i}"], err_msg=f"encode {c}")
+        kd, vd = gpu_decode(ext, torch.from_numpy(arrays[f"blobs{i}"]), toks, tuple(k.shape), c["rope"], c["mla"],
+                            c["material"])
+        np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), arrays[f"kdec{i}"].reshape(kd.shape),
+                                      err_msg=f"decode {c}")
+        if not c["mla"]:
+            np.testing.assert_array_equal(vd.cpu().numpy().view(np.uint16), arrays[f"vdec{i}"].reshape(vd.shape))
+
+
+@pytest.mark.parametrize("case", helpers.load_json("codec_digests.json"), ids=lambda c: c["name"])
+def test_full_size_digests_bf16_input(ext, case):
+    kb, vb, k16, v16, m, toks, shape = helpers.full_case_inputs(case)
+    blobs = gpu_encode(ext, kb, vb, torch.from_numpy(toks), shape.rope_dim, case["preset"], case["rope_mode"],
+                       case["expected_payload"], m)
+    assert blobs.shape[1] == case["blob_bytes"]
+    assert helpers.sha(blobs.cpu().numpy()) == case["blobs_sha256"]
+    # the fp16 path must produce the same bytes as bf16 rounded to fp16
+    blobs16 = gpu_encode(ext, k16, v16, torch.from_numpy(toks), shape.rope_dim, case["preset"], case["rope_mode"],
+                         case["expected_payload"], m)
+    assert torch.equal(blobs, blobs16)
+    kd, vd = gpu_decode(ext, blobs, torch.from_numpy(toks), tuple(k16.shape), shape.rope_dim, shape.mla, m)
+    assert helpers.sha(kd.cpu().numpy()) == case["k_decoded_sha256"]
+    if vd is not None:
+        assert helpers.sha(vd.cpu().numpy()) == case["v_decoded_sha256"]
+
+
+def test_config0_256_pages_bit_exact(ext, oracle):
+    """BASELINE config 0 at full size: 256 GQA pages, INT4_SYM + PRESERVE_FP8, bf16 input."""
+    from ztcp_b200 import workload
+
+    k32, v32 = workload.kv_pages_np(256, workload.GQA, seed=42)
+    kb, vb = torch.from_numpy(k32).to(torch.bfloat16), torch.from_numpy(v32).to(torch.bfloat16)
+    m = workload.session_material(7)
+    toks = workload.token_hashes(256, 11)
+    exp = 98304
+    blobs = gpu_encode(ext, kb, vb, torch.from_numpy(toks), 64, 1, 1, exp, m)
+    want = helpers.oracle_encode(oracle, kb.half().numpy(), vb.half().numpy(), toks, 64, 1, 1, exp, m)
+    np.testing.assert_array_equal(blobs.cpu().numpy(), want)
+    kd, vd = gpu_decode(ext, blobs, torch.from_numpy(toks), tuple(kb.shape), 64, False, m)
+    okd, ovd, st, first = helpers.oracle_decode(oracle, want, toks, tuple(kb.shape), 64, False, m)
+    assert first == -1
+    np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd)
+    np.testing.assert_array_equal(vd.cpu().numpy().view(np.uint16), ovd)
+
+
+@pytest.mark.parametrize("T,H,D,rope,extra", [(7, 3, 48, 16, 1), (100, 1, 64, 32, 3), (5, 2, 16, 16, 13),
+                                               (130, 1, 32, 0, 6), (1, 1, 16, 0, 0)])
+def test_ragged_geometry_and_misaligned_blobs(ext, oracle, T, H, D, rope, extra):
+    """Tiles that do not divide the page, byte ranges off 64-byte blocks, and blob strides that are not
+    multiples of 16 (or of 4) exercise the byte-granular paths."""
+    from ztcp_b200 import workload
+
+    rng = np.random.default_rng(T * 1000 + D)
+    for preset in (1, 2, 3):
+        for rope_mode in (0, 1, 2):
+            for mla in (False, True):
+                k = rng.standard_normal((3, T, H, D)).astype(np.float16)
+                v = None if mla else rng.standard_normal((3, T, H, D)).astype(np.float16)
+                m = workload.session_material(int(rng.integers(1 << 30)))
+                toks = workload.token_hashes(3, int(rng.integers(1 << 30)))
+                exp = oracle.spec_payload_bytes(preset, rope_mode, T * H, D, rope, not mla) + extra
+                blobs = gpu_encode(ext, torch.from_numpy(k), None if v is None else torch.from_numpy(v),
+                                   torch.from_numpy(toks), rope, preset, rope_mode, exp, m)
+                want = helpers.oracle_encode(oracle, k, v, toks, rope, preset, rope_mode, exp, m)
+                np.testing.assert_array_equal(blobs.cpu().numpy(), want, err_msg=f"{preset} {rope_mode} {mla}")
+                kd, vd = gpu_decode(ext, blobs, torch.from_numpy(toks), k.shape, rope, mla, m)
+                okd, ovd, _, first = helpers.oracle_decode(oracle, want, toks, k.shape, rope, mla, m)
+                assert first == -1
+                np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd)
+                if not mla:
+                    np.testing.assert_array_equal(vd.cpu().numpy().view(np.uint16), ovd)
+
+
+def test_block_table_and_per_page_metadata(oracle):
+    """Shuffled block table over a KV pool with per-page layer ids and sequence nonces (the offload sweep's
+    addressing); each blob must equal the oracle's single-page encode of the addressed block."""
+    from ztcp_b200 import capi, codec, workload
+
+    rng = np.random.default_rng(4)
+    pool = 40
+    k32, v32 = workload.kv_pages_np(pool, workload.GQA, seed=8)
+    kb = torch.from_numpy(k32).to(torch.bfloat16).to(DEV)
+    vb = torch.from_numpy(v32).to(torch.bfloat16).to(DEV)
+    n = 24
+    table = rng.permutation(pool)[:n].astype(np.int32)
+    layers = rng.integers(0, 64, n).astype(np.int16)
+    seqs = rng.integers(0, 2**62, n).astype(np.int64)
+    toks = workload.token_hashes(n, 3)
+    m = workload.session_material(12)
+    keys = capi.keys(*m["key"], *m["mac_key"])
+    out = torch.empty((n, 98352), dtype=torch.uint8, device=DEV)
+    codec.encode_pages(kb, vb, torch.from_numpy(toks).to(DEV), out, rope_dim=64, preset=1, rope_mode=1,
+                       expected_payload_bytes=98304, tenant_id_hash=m["tenant"], model_id_hash=m["model"],
+                       layer_id=0, head_group_id=m["head_group"], base_sequence_nonce=0, keys=keys,
+                       block_table=torch.from_numpy(table).to(DEV), sequence_nonces=torch.from_numpy(seqs).to(DEV),
+                       layer_ids=torch.from_numpy(layers).to(DEV))
+    got = out.cpu().numpy()
+    k16 = kb.half().cpu().numpy()
+    v16 = vb.half().cpu().numpy()
+    for i in range(n):
+        mi = dict(m, layer=int(layers[i]), base_seq=int(seqs[i]))
+        want = helpers.oracle_encode(oracle, k16[table[i]][None], v16[table[i]][None], toks[i:i + 1], 64, 1, 1, 98304,
+                                     mi)
+        np.testing.assert_array_equal(got[i], want[0], err_msg=f"page {i}")
+    # decode back into a fresh pool through the same table, per-page expected layers
+    kout = torch.zeros((pool, 64, 8, 128), dtype=torch.float16, device=DEV)
+    vout = torch.zeros_like(kout)
+    st, fail = codec.decode_pages(out, torch.from_numpy(toks).to(DEV), kout, vout, rope_dim=64, is_mla=False,
+                                  tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=0, keys=keys,
+                                  block_table=torch.from_numpy(table).to(DEV),
+                                  layer_ids=torch.from_numpy(layers).to(DEV))
+    codec.raise_for_status(st, fail)
+    for i in range(n):
+        mi = dict(m, layer=int(layers[i]))
+        okd, ovd, _, first = helpers.oracle_decode(oracle, got[i:i + 1], toks[i:i + 1], (1, 64, 8, 128), 64, False, mi)
+        assert first == -1
+        np.testing.assert_array_equal(kout[table[i]].cpu().numpy().view(np.uint16), okd[0])
+        np.testing.assert_array_equal(vout[table[i]].cpu().numpy().view(np.uint16), ovd[0])
+    untouched = np.setdiff1d(np.arange(pool), table)
+    assert not kout[torch.from_numpy(untouched).to(DEV).long()].any()
+
+
+def _encoded_batch(ext, n=6):
+    from ztcp_b200 import workload
+
+    k32, v32 = workload.kv_pages_np(n, workload.GQA, seed=21)
+    kb, vb = torch.from_numpy(k32).to(torch.bfloat16), torch.from_numpy(v32).to(torch.bfloat16)
+    m = workload.session_material(22)
+    toks = torch.from_numpy(workload.token_hashes(n, 23))
+    return gpu_encode(ext, kb, vb, toks, 64, 1, 1, 98304, m), toks, m, kb
+
+
+def _expect_batch_failure(ext, blobs, toks, m, msg, **over):
+    mm = dict(m, **over)
+    k = torch.full((blobs.shape[0], 64, 8, 128), 3.0, dtype=torch.float16, device=DEV)
+    v = torch.full_like(k, 3.0)
+    with pytest.raises(RuntimeError, match=msg):
+        ext.fused_decode_cold_pages_peak_into_cpu(blobs, toks.to(DEV), k, v, 64, False, mm["tenant"], mm["model"],
+                                                  mm["layer"], **_keys(mm))
+    assert not k.any() and not v.any(), "a failed batch must zero every output page"
+
+
+def test_tamper_and_aad_statuses(ext, oracle):
+    blobs, toks, m, _ = _encoded_batch(ext)
+    # reference tamper offsets for GQA INT4+FP8 (bench:318-377): scale byte, 16-byte NoPE swap, paired V flips
+    vecs, gs, r, nd = 512, 16, 64, 64
+    s_rope = 32 + vecs * r
+    q_nope = s_rope + vecs * (r // gs) * 2
+    q_v = q_nope + vecs * (nd // 2) + vecs * (nd // gs) * 2
+    for mutate in (lambda b: b.__setitem__((3, s_rope), b[3, s_rope] ^ 1),
+                   lambda b: b.__setitem__((1, slice(q_nope, q_nope + 32)),
+                                           torch.cat([b[1, q_nope + 16:q_nope + 32], b[1, q_nope:q_nope + 16]])),
+                   lambda b: (b.__setitem__((5, q_v), b[5, q_v] ^ 1), b.__setitem__((5, q_v + 16), b[5, q_v + 16] ^ 1)),
+                   lambda b: b.__setitem__((0, 64), b[0, 64] ^ 1),
+                   lambda b: b.__setitem__((2, -1), b[2, -1] ^ 0x80)):
+        bad = blobs.clone()
+        mutate(bad)
+        _expect_batch_failure(ext, bad, toks, m, "KV_INTEGRITY_ERROR: Cold-page MAC verification failed")
+    for over in (dict(tenant=m["tenant"] ^ 1), dict(model=m["model"] ^ 2), dict(layer=m["layer"] ^ 4)):
+        _expect_batch_failure(ext, blobs, toks, m, "CROSS_TENANT_CONTAMINATION", **over)
+    t2 = toks.clone()
+    t2[4] ^= 1
+    _expect_batch_failure(ext, blobs, t2, m, "CROSS_TENANT_CONTAMINATION")
+    bad = blobs.clone()
+    bad[2, 0] ^= 1
+    _expect_batch_failure(ext, bad, toks, m, "Invalid cold-page header magic, version, or flags")
+    # forged flags / truncated payload with valid tags -> the flags statuses (4, 5)
+    forged = blobs.clone()
+    forged[1, 3] = 0x04
+    tag = oracle.siphash24_128(forged[1, :-16].cpu().numpy().tobytes(), *m["mac_key"])
+    forged[1, -16:] = torch.tensor(list(tag), dtype=torch.uint8)
+    _expect_batch_failure(ext, forged, toks, m, "Invalid cold-page header magic, version, or flags")
+    # single-page API raises the single-page texts
+    with pytest.raises(RuntimeError, match="Invalid cold-page header flags"):
+        ext.fused_decode_cold_page_cpu(forged[1].contiguous(), 64, 8, 128, 64, False, m["tenant"], m["model"],
+                                       m["layer"], int(toks[1]), **_keys(m))
+    short = torch.cat([blobs[:, :32 + 1000], blobs[:, -16:]], dim=1).contiguous()
+    for b in range(short.shape[0]):
+        tag = oracle.siphash24_128(short[b, :-16].cpu().numpy().tobytes(), *m["mac_key"])
+        short[b, -16:] = torch.tensor(list(tag), dtype=torch.uint8)
+    with pytest.raises(RuntimeError, match="payload truncated"):
+        ext.fused_decode_cold_page_cpu(short[0].contiguous(), 64, 8, 128, 64, False, m["tenant"], m["model"],
+                                       m["layer"], int(toks[0]), **_keys(m))
+
+
+def test_host_placement_dropin(ext, oracle):
+    """CPU tensors in and out (the reference wrapper's placement): staged through the GPU, same bytes."""
+    from ztcp_b200 import workload
+
+    k32, v32 = workload.kv_pages_np(3, workload.GQA, seed=31)
+    k16 = torch.from_numpy(k32).half()
+    v16 = torch.from_numpy(v32).half()
+    m = workload.session_material(32)
+    toks = torch.from_numpy(workload.token_hashes(3, 33))
+    blobs = ext.fused_encode_cold_pages_batch_cpu(k16, v16, toks, 2, 1, 64, 114688, m["tenant"], m["model"],
+                                                  m["layer"], m["head_group"], m["base_seq"], **_keys(m))
+    assert blobs.device.type == "cpu"
+    want = helpers.oracle_encode(oracle, k16.numpy(), v16.numpy(), toks.numpy(), 64, 2, 1, 114688, m)
+    np.testing.assert_array_equal(blobs.numpy(), want)
+    k, v = ext.fused_decode_cold_pages_batch_cpu(blobs, toks, 64, 8, 128, 64, False, m["tenant"], m["model"],
+                                                 m["layer"], **_keys(m))
+    okd, ovd, _, _ = helpers.oracle_decode(oracle, want, toks.numpy(), (3, 64, 8, 128), 64, False, m)
+    np.testing.assert_array_equal(k.numpy().view(np.uint16), okd)
+    one = ext.fused_encode_cold_page_cpu(k16[1], v16[1], 2, 1, 64, 114688, m["tenant"], m["model"], m["layer"],
+                                         m["head_group"], int(toks[1]), m["base_seq"] + 1, **_keys(m))
+    np.testing.assert_array_equal(one.numpy(), want[1])
+    k1, v1 = ext.fused_decode_cold_page_cpu(one, 64, 8, 128, 64, False, m["tenant"], m["model"], m["layer"],
+                                            int(toks[1]), **_keys(m))
+    np.testing.assert_array_equal(k1.numpy().view(np.uint16), okd[1])
+
+
+def test_fidelity_configs_2_and_3(ext):
+    """Attention-output cosine (GQA, 32 queries/head, seed 99) and softmax-weights cosine (MLA, 16 query heads)."""
+    from ztcp_b200 import workload
+
+    k32, v32 = workload.kv_pages_np(16, workload.GQA, seed=42)
+    kb, vb = torch.from_numpy(k32).to(torch.bfloat16), torch.from_numpy(v32).to(torch.bfloat16)
+    m = workload.session_material(7)
+    toks = torch.from_numpy(workload.token_hashes(16, 11))
+    blobs = gpu_encode(ext, kb, vb, toks, 64, 1, 1, 98304, m)
+    kd, vd = gpu_decode(ext, blobs, toks, tuple(kb.shape), 64, False, m)
+    cos = helpers.attention_output_cosine(kb.float(), vb.float(), kd.cpu().float(), vd.cpu().float(), 32)
+    assert cos > 0.99, cos
+    k32, _ = workload.kv_pages_np(16, workload.MLA, seed=42)
+    kb = torch.from_numpy(k32).to(torch.bfloat16)
+    blobs = gpu_encode(ext, kb, None, toks, 64, 1, 1, 25088, m)
+    kd, _ = gpu_decode(ext, blobs, toks, tuple(kb.shape), 64, True, m)
+    cos = helpers.attention_output_cosine(kb.float(), None, kd.cpu().float(), None, 16)
+    assert cos > 0.99, cos

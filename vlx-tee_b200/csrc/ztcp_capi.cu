@@ -1,0 +1,250 @@
+// ztcp_capi.cu -- host layer of the C-ABI declared in include/ztcp_b200.h.
+//
+// Validates arguments with the reference's TORCH_CHECK rules and messages (csrc:1499-1507,
+// 1925-1957, 2269-2296), plans the tiling and launches the kernels on the caller's stream.  Nothing
+// here allocates device memory or synchronizes.
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <string>
+
+#include "../../include/ztcp_b200.h"
+#include "ztcp_kernels.cuh"
+#include "ztcp_layout.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+// Shared memory one tile may stage (the sm_100 opt-in limit is 227 KB per CTA).
+constexpr int64_t kMaxStageBytes = 200 * 1024;
+
+int32_t fail(int32_t code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Geometry rule of the reference (csrc:1507, :1930): positive tokens/heads, head_dim a positive multiple
+// of 16, rope_dim a multiple of 16 in [0, head_dim].
+int32_t check_geometry(const ztcp_geometry* g, const char* dims_msg) {
+  if (!g) return fail(ZTCP_EINVAL, "geometry must not be NULL");
+  if (!(g->num_tokens > 0 && g->num_heads > 0 && g->head_dim >= 16 && (g->head_dim % 16) == 0))
+    return fail(ZTCP_EINVAL, dims_msg);
+  if (!(g->rope_dim >= 0 && g->rope_dim <= g->head_dim && (g->rope_dim % 16) == 0))
+    return fail(ZTCP_EINVAL, "Invalid rope_dim");
+  const int64_t vecs = g->num_tokens * g->num_heads;
+  if (vecs > (int64_t)1 << 31 || g->head_dim > (int64_t)1 << 20) return fail(ZTCP_EINVAL, "KV page geometry too large");
+  return ZTCP_OK;
+}
+
+int32_t check_batch(const ztcp_page_batch* b) {
+  if (!b) return fail(ZTCP_EINVAL, "page batch must not be NULL");
+  if (b->n_pages <= 0) return fail(ZTCP_EINVAL, "batch must hold at least one page");
+  if (!b->token_hash) return fail(ZTCP_EINVAL, "page_token_hashes must not be NULL");
+  return ZTCP_OK;
+}
+
+ztcp::PageMeta to_meta(const ztcp_page_batch* b) {
+  ztcp::PageMeta m;
+  m.kv_block = b->kv_block;
+  m.token_hash = b->token_hash;
+  m.sequence_nonce = b->sequence_nonce;
+  m.layer_id = b->layer_id;
+  m.seq_base = b->base_sequence_nonce;
+  m.tenant = b->tenant_id_hash;
+  m.model = b->model_id_hash;
+  m.layer_uniform = b->layer_id_uniform;
+  m.head_group = b->head_group_id;
+  return m;
+}
+
+void key_words(const ztcp_keys* k, uint32_t out[8]) {
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = (uint32_t)k->enc[i];
+    out[2 * i + 1] = (uint32_t)(k->enc[i] >> 32);
+  }
+}
+
+// Vecs per CTA tile: 64 rows (a whole page when it is smaller), fewer when the staging would exceed
+// 96 KB of shared memory.
+int32_t pick_tile_vecs(int64_t vecs, int64_t stage_per_vec) {
+  int64_t tv = vecs < 64 ? vecs : 64;
+  while (tv > 1 && tv * stage_per_vec > 96 * 1024) tv = (tv + 1) / 2;
+  return (int32_t)tv;
+}
+
+int32_t launch_status(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(ZTCP_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  return ZTCP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* ztcp_last_error(void) { return g_last_error.c_str(); }
+
+int32_t ztcp_version(void) { return 100; }
+
+int64_t ztcp_min_payload_bytes(int32_t preset, int32_t rope_mode, const ztcp_geometry* geom, int32_t has_v) {
+  if (!geom) return -1;
+  ztcp::Layout L;
+  if (!ztcp::build_layout(preset, rope_mode, geom->num_tokens * geom->num_heads, geom->head_dim, geom->rope_dim,
+                          has_v != 0, &L))
+    return -1;
+  return L.data_end;
+}
+
+int64_t ztcp_spec_payload_bytes(int32_t preset, int32_t rope_mode, const ztcp_geometry* geom, int32_t has_v) {
+  if (!geom) return -1;
+  return ztcp::spec_payload_bytes(preset, rope_mode, geom->num_tokens * geom->num_heads, geom->head_dim,
+                                  geom->rope_dim, has_v != 0);
+}
+
+int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_dtype, const ztcp_geometry* geom,
+                          const ztcp_page_batch* batch, int32_t preset, int32_t rope_mode,
+                          int64_t expected_payload_bytes, const ztcp_keys* keys, uint8_t* out_blobs, void* stream) {
+  int32_t rc = check_geometry(geom, "Invalid k_pages dimensions");
+  if (rc != ZTCP_OK) return rc;
+  if ((rc = check_batch(batch)) != ZTCP_OK) return rc;
+  if (!keys) return fail(ZTCP_EINVAL, "keys must not be NULL");
+  if (!k_pages || !out_blobs) return fail(ZTCP_EINVAL, "k_pages and out_blobs must not be NULL");
+  if (kv_dtype != ZTCP_DTYPE_F16 && kv_dtype != ZTCP_DTYPE_BF16)
+    return fail(ZTCP_EINVAL, "k_pages must be float16 or bfloat16");
+  if (!aligned16(k_pages) || (v_pages && !aligned16(v_pages)))
+    return fail(ZTCP_EINVAL, "k_pages / v_pages must be 16-byte aligned");
+  if (preset < 1 || preset > 3) return fail(ZTCP_EINVAL, "Invalid preset (must be 1..3)");
+  if (rope_mode < 0 || rope_mode > 2) return fail(ZTCP_EINVAL, "Invalid rope_mode (must be 0..2)");
+  const int64_t vecs = geom->num_tokens * geom->num_heads;
+  ztcp::EgressParams P;
+  memset(&P, 0, sizeof(P));
+  ztcp::build_layout(preset, rope_mode, vecs, geom->head_dim, geom->rope_dim, v_pages != nullptr, &P.L);
+  if (expected_payload_bytes < P.L.data_end)
+    return fail(ZTCP_EINVAL, "expected_payload_bytes smaller than required payload");
+  if (expected_payload_bytes > ((int64_t)1 << 36))
+    return fail(ZTCP_EINVAL, "expected_payload_bytes too large");
+  P.k = static_cast<const uint16_t*>(k_pages);
+  P.v = static_cast<const uint16_t*>(v_pages);
+  P.page_elems = vecs * geom->head_dim;
+  P.out = out_blobs;
+  P.blob_stride = ztcp::kHeaderBytes + expected_payload_bytes + ztcp::kTagBytes;
+  P.payload_len = expected_payload_bytes;
+  P.vecs = vecs;
+  P.head_dim = (int32_t)geom->head_dim;
+  P.flags = (preset & 0x0F) | ((rope_mode & 0x0F) << 4);
+  P.meta = to_meta(batch);
+  key_words(keys, P.key);
+  P.tile_vecs = pick_tile_vecs(vecs, ztcp::stage_bytes_per_vec(P.L));
+  P.n_tiles = (int32_t)((vecs + P.tile_vecs - 1) / P.tile_vecs);
+  P.n_pages = batch->n_pages;
+  P.stage_bytes = ztcp::plan_stage(P.L, P.tile_vecs, P.stage_q, P.stage_s);
+  if (P.stage_bytes > kMaxStageBytes) return fail(ZTCP_EINVAL, "head_dim too large for one tile");
+  if (P.n_pages * P.n_tiles > 0x7FFFFFFFLL) return fail(ZTCP_EINVAL, "batch too large for one launch");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ztcp::launch_egress(P, kv_dtype == ZTCP_DTYPE_BF16, s);
+  if ((rc = launch_status("egress_tile_kernel")) != ZTCP_OK) return rc;
+
+  ztcp::MacParams M;
+  memset(&M, 0, sizeof(M));
+  M.blobs = out_blobs;
+  M.blob_stride = P.blob_stride;
+  M.payload_len = expected_payload_bytes;
+  M.n_pages = batch->n_pages;
+  M.mk0 = keys->mac[0];
+  M.mk1 = keys->mac[1];
+  ztcp::launch_mac(M, false, s);
+  return launch_status("mac_kernel<sign>");
+}
+
+int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_geometry* geom,
+                          const ztcp_page_batch* batch, const ztcp_keys* keys, uint16_t* out_k, uint16_t* out_v,
+                          int32_t* status, int32_t* any_fail, void* stream) {
+  int32_t rc = check_geometry(geom, "Invalid out_k_pages dimensions");
+  if (rc != ZTCP_OK) return rc;
+  if ((rc = check_batch(batch)) != ZTCP_OK) return rc;
+  if (!keys) return fail(ZTCP_EINVAL, "keys must not be NULL");
+  if (!blobs || !out_k || !status || !any_fail)
+    return fail(ZTCP_EINVAL, "cold_blobs, out_k_pages, status and any_fail must not be NULL");
+  if (blob_bytes <= ztcp::kHeaderBytes + ztcp::kTagBytes) return fail(ZTCP_EINVAL, "cold_blob too small");
+  const bool has_v = geom->is_mla_single_buffer == 0;
+  if (has_v && !out_v) return fail(ZTCP_EINVAL, "out_v_pages is required for non-MLA geometry");
+  if (!has_v && out_v) return fail(ZTCP_EINVAL, "out_v_pages must be NULL for a single-buffer MLA geometry");
+  if (!aligned16(out_k) || (out_v && !aligned16(out_v)))
+    return fail(ZTCP_EINVAL, "out_k_pages / out_v_pages must be 16-byte aligned");
+  const int64_t vecs = geom->num_tokens * geom->num_heads;
+  const int64_t payload_len = blob_bytes - ztcp::kHeaderBytes - ztcp::kTagBytes;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  ztcp::MacParams M;
+  memset(&M, 0, sizeof(M));
+  M.blobs = const_cast<uint8_t*>(blobs);
+  M.blob_stride = blob_bytes;
+  M.payload_len = payload_len;
+  M.n_pages = batch->n_pages;
+  M.mk0 = keys->mac[0];
+  M.mk1 = keys->mac[1];
+  M.meta = to_meta(batch);
+  M.vecs = vecs;
+  M.head_dim = geom->head_dim;
+  M.rope_dim = geom->rope_dim;
+  M.has_v = has_v;
+  M.status = status;
+  M.any_fail = any_fail;
+
+  ztcp::IngressParams P;
+  memset(&P, 0, sizeof(P));
+  P.blobs = blobs;
+  P.blob_stride = blob_bytes;
+  P.payload_len = payload_len;
+  P.k_out = out_k;
+  P.v_out = out_v;
+  P.page_elems = vecs * geom->head_dim;
+  P.vecs = vecs;
+  P.head_dim = (int32_t)geom->head_dim;
+  P.rope_dim = (int32_t)geom->rope_dim;
+  P.has_v = has_v;
+  P.meta = to_meta(batch);
+  key_words(keys, P.key);
+  P.any_fail = any_fail;
+  const int64_t worst = ztcp::worst_stage_bytes_per_vec(geom->head_dim, geom->rope_dim, has_v);
+  P.tile_vecs = pick_tile_vecs(vecs, worst);
+  P.n_tiles = (int32_t)((vecs + P.tile_vecs - 1) / P.tile_vecs);
+  P.n_pages = batch->n_pages;
+  // worst case over every (preset, rope_mode) a header may carry, plus 16-byte rounding per area
+  if (P.tile_vecs * worst + 6 * 16 > kMaxStageBytes) return fail(ZTCP_EINVAL, "head_dim too large for one tile");
+  P.stage_bytes = (int32_t)(P.tile_vecs * worst + 6 * 16);
+  if (P.n_pages * P.n_tiles > 0x7FFFFFFFLL) return fail(ZTCP_EINVAL, "batch too large for one launch");
+
+  if (cudaMemsetAsync(any_fail, 0, sizeof(int32_t), s) != cudaSuccess) return launch_status("memset any_fail");
+  ztcp::launch_mac(M, true, s);
+  if ((rc = launch_status("mac_kernel<verify>")) != ZTCP_OK) return rc;
+  ztcp::launch_ingress(P, s);
+  return launch_status("ingress_tile_kernel");
+}
+
+int32_t ztcp_chacha20_xor(const uint8_t* src, uint8_t* dst, int64_t len, const uint8_t key32[32], uint32_t counter,
+                          const uint8_t nonce12[12], void* stream) {
+  if (len < 0) return fail(ZTCP_EINVAL, "len must be non-negative");
+  if (!key32 || !nonce12) return fail(ZTCP_EINVAL, "key_u8 must be 32-byte and nonce_u8 12-byte");
+  if (len == 0) return ZTCP_OK;
+  if (!src || !dst) return fail(ZTCP_EINVAL, "data must not be NULL");
+  uint32_t key[8], nonce[3];
+  memcpy(key, key32, 32);
+  memcpy(nonce, nonce12, 12);
+  ztcp::launch_chacha20_xor(src, dst, len, key, counter, nonce, static_cast<cudaStream_t>(stream));
+  return launch_status("chacha20_xor_kernel");
+}
+
+int32_t ztcp_siphash24_128(const uint8_t* src, int64_t len, uint64_t mk0, uint64_t mk1, uint8_t* out16,
+                           void* stream) {
+  if (len < 0) return fail(ZTCP_EINVAL, "len must be non-negative");
+  if (!out16 || (len > 0 && !src)) return fail(ZTCP_EINVAL, "data and out must not be NULL");
+  ztcp::launch_siphash(src, len, mk0, mk1, out16, static_cast<cudaStream_t>(stream));
+  return launch_status("siphash_kernel");
+}
+
+}  // extern "C"

@@ -1,0 +1,500 @@
+// ztcp_kernels.cu -- sm_100a kernels of the ZTCP cold-page codec.
+//
+// Egress  = egress_tile_kernel (quantize + pack + ChaCha20, per (page, vec-tile))
+//         + mac_kernel<sign>    (one SipHash-2-4-128 chain per lane = per page, writes the tag)
+// Ingress = mac_kernel<verify>  (header / AAD / tag / flags checks, per-page status, batch fail flag)
+//         + ingress_tile_kernel (decrypt + dequantize per (page, vec-tile); zeroes every output when
+//                                any page of the batch failed -- the reference's all-or-nothing rule,
+//                                csrc:2481-2495)
+//
+// Tiling.  A CTA owns `tile_vecs` consecutive vecs (token x head rows) of one page.  Those rows map
+// to one contiguous byte range per q region and per scale region of every section (the payload is
+// vec-major within a region), so a CTA quantizes its rows into shared memory and then encrypts its
+// own byte ranges.  ChaCha20 is counter-indexed (payload byte x uses block 1 + x / 64), so every
+// 64-byte keystream block is computed by exactly the threads that need it; a block straddling two
+// tiles is computed by both and each writes only its own bytes.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "ztcp_device.cuh"
+#include "ztcp_kernels.cuh"
+
+namespace ztcp {
+
+namespace {
+
+__device__ __forceinline__ int64_t page_block(const PageMeta& m, int64_t page) {
+  return m.kv_block ? (int64_t)m.kv_block[page] : page;
+}
+__device__ __forceinline__ uint64_t page_seq(const PageMeta& m, int64_t page) {
+  return m.sequence_nonce ? m.sequence_nonce[page] : m.seq_base + (uint64_t)page;
+}
+__device__ __forceinline__ uint16_t page_layer(const PageMeta& m, int64_t page) {
+  return m.layer_id ? m.layer_id[page] : m.layer_uniform;
+}
+
+__device__ __forceinline__ Section pick(const Layout& L, int s) {
+  return s == 0 ? L.sec[0] : (s == 1 ? L.sec[1] : L.sec[2]);
+}
+
+// A payload byte range [a, b) owned by one tile, backed by shared-memory staging (or zeros).
+struct Range {
+  int64_t a, b;
+  int32_t stage;
+  int32_t zero;
+};
+
+__device__ __forceinline__ int tile_ranges(const Layout& L, int64_t v0, int tv, const int32_t sq[3],
+                                           const int32_t ss[3], bool with_pad, int64_t payload_len, Range r[7]) {
+  int n = 0;
+#pragma unroll
+  for (int s = 0; s < 3; ++s) {
+    if (s >= L.n) break;
+    const Section S = pick(L, s);
+    r[n++] = Range{S.q_off + v0 * S.q_bpv, S.q_off + (v0 + tv) * S.q_bpv, sq[s], 0};
+    if (S.kind != kRaw) r[n++] = Range{S.s_off + v0 * S.s_bpv, S.s_off + (v0 + tv) * S.s_bpv, ss[s], 0};
+  }
+  if (with_pad && payload_len > L.data_end) r[n++] = Range{L.data_end, payload_len, 0, 1};
+  return n;
+}
+
+__device__ __forceinline__ int64_t range_blocks(const Range& r) {
+  return r.b > r.a ? ((r.b - 1) >> 6) - (r.a >> 6) + 1 : 0;
+}
+
+__device__ __forceinline__ uint32_t pack2(uint16_t a, uint16_t b) { return (uint32_t)a | ((uint32_t)b << 16); }
+
+// XOR one keystream block into bytes [lo, hi) of dst, taking plaintext from src (nullptr = zeros).
+// Both pointers address payload byte 64*kb (block start); bytes outside [lo, hi) are untouched.
+__device__ __forceinline__ void xor_block_bytes(uint8_t* dst, const uint8_t* src, const uint32_t ks[16], int lo,
+                                                int hi) {
+#pragma unroll
+  for (int w = 0; w < 16; ++w) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int x = 4 * w + j;
+      if (x >= lo && x < hi) dst[x] = (uint8_t)((src ? src[x] : 0) ^ (uint8_t)(ks[w] >> (8 * j)));
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Egress: quantize + pack + encrypt one (page, vec-tile)
+// ------------------------------------------------------------------------------------------------
+template <bool BF16>
+__global__ void __launch_bounds__(kTileThreads) egress_tile_kernel(const __grid_constant__ EgressParams P) {
+  extern __shared__ __align__(16) uint8_t stage[];
+  const int64_t page = blockIdx.x / P.n_tiles;
+  const int tile = (int)(blockIdx.x - page * P.n_tiles);
+  const int64_t v0 = (int64_t)tile * P.tile_vecs;
+  const int tv = (int)min((int64_t)P.tile_vecs, P.vecs - v0);
+  const int64_t blk = page_block(P.meta, page);
+  const uint16_t* kp = P.k + blk * P.page_elems;
+  const uint16_t* vp = P.v ? P.v + blk * P.page_elems : nullptr;
+
+  // ---- phase 1: quantize this tile's rows of every section into shared memory
+  int items[3] = {0, 0, 0};
+  int total = 0;
+#pragma unroll
+  for (int s = 0; s < 3; ++s)
+    if (s < P.L.n) {
+      items[s] = tv * (pick(P.L, s).dim >> 4);
+      total += items[s];
+    }
+  for (int it = threadIdx.x; it < total; it += blockDim.x) {
+    int s = 0, local = it;
+    if (local >= items[0]) { local -= items[0]; s = 1; if (local >= items[1]) { local -= items[1]; s = 2; } }
+    const Section S = pick(P.L, s);
+    const int groups = S.dim >> 4;
+    const int vec = local / groups, g = local - vec * groups;
+    const uint16_t* src = (S.buf ? vp : kp) + (v0 + vec) * P.head_dim + S.col + g * 16;
+    uint16_t h[16];
+    load_group16<BF16>(src, h);
+    uint8_t* qd = stage + (s == 0 ? P.stage_q[0] : (s == 1 ? P.stage_q[1] : P.stage_q[2])) + vec * S.q_bpv;
+    uint8_t* sd = stage + (s == 0 ? P.stage_s[0] : (s == 1 ? P.stage_s[1] : P.stage_s[2])) + vec * S.s_bpv;
+    if (S.kind == kRaw) {
+      uint4* d = reinterpret_cast<uint4*>(qd + g * 32);
+      d[0] = make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]), pack2(h[6], h[7]));
+      d[1] = make_uint4(pack2(h[8], h[9]), pack2(h[10], h[11]), pack2(h[12], h[13]), pack2(h[14], h[15]));
+    } else if (S.kind == kInt8) {
+      uint32_t q[4];
+      const uint16_t sc = quant_int8(h, q);
+      *reinterpret_cast<uint4*>(qd + g * 16) = make_uint4(q[0], q[1], q[2], q[3]);
+      *reinterpret_cast<uint16_t*>(sd + g * 2) = sc;
+    } else {
+      uint32_t q[2];
+      const uint16_t sc = quant_int4(h, q);
+      *reinterpret_cast<uint2*>(qd + g * 8) = make_uint2(q[0], q[1]);
+      *reinterpret_cast<uint16_t*>(sd + g * 2) = sc;
+    }
+  }
+
+  // header (32 bytes) by tile 0
+  uint8_t* blob = P.out + page * P.blob_stride;
+  const uint64_t seq = page_seq(P.meta, page);
+  const uint16_t layer = page_layer(P.meta, page);
+  if (tile == 0 && threadIdx.x == 0) {
+    const uint64_t tok = P.meta.token_hash[page];
+    const uint32_t hw[8] = {(uint32_t)kMagic | ((uint32_t)kVersion << 16) | ((uint32_t)P.flags << 24),
+                            P.meta.tenant,
+                            P.meta.model,
+                            (uint32_t)layer | ((uint32_t)P.meta.head_group << 16),
+                            (uint32_t)tok,
+                            (uint32_t)(tok >> 32),
+                            (uint32_t)seq,
+                            (uint32_t)(seq >> 32)};
+    if ((reinterpret_cast<uintptr_t>(blob) & 3) == 0) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) reinterpret_cast<uint32_t*>(blob)[i] = hw[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) blob[i] = (uint8_t)(hw[i >> 2] >> (8 * (i & 3)));
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 2: encrypt this tile's byte ranges
+  Range R[7];
+  const int nr = tile_ranges(P.L, v0, tv, P.stage_q, P.stage_s, tile == P.n_tiles - 1, P.payload_len, R);
+  int64_t nb[7];
+  int64_t total_blocks = 0;
+#pragma unroll
+  for (int i = 0; i < 7; ++i) {
+    nb[i] = i < nr ? range_blocks(R[i]) : 0;
+    total_blocks += nb[i];
+  }
+  const uint32_t n2 = ((uint32_t)layer << 16) | P.meta.head_group;
+  uint8_t* payload = blob + kHeaderBytes;
+  for (int64_t bi = threadIdx.x; bi < total_blocks; bi += blockDim.x) {
+    int i = 0;
+    int64_t local = bi;
+    while (i < nr - 1 && local >= nb[i]) { local -= nb[i]; ++i; }
+    const Range r = R[i];
+    const int64_t kb = (r.a >> 6) + local;
+    uint32_t ks[16];
+    chacha20_block(P.key, (uint32_t)(1 + kb), (uint32_t)seq, (uint32_t)(seq >> 32), n2, ks);
+    const int64_t base = kb << 6;
+    const int lo = (int)(max(r.a, base) - base), hi = (int)(min(r.b, base + 64) - base);
+    uint8_t* dst = payload + base;
+    const uint8_t* src = r.zero ? nullptr : stage + r.stage + (base - r.a);  // only bytes [lo, hi) are read
+    const bool full = lo == 0 && hi == 64;
+    if (full && ((reinterpret_cast<uintptr_t>(dst) | (r.zero ? 0 : reinterpret_cast<uintptr_t>(src))) & 15) == 0) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint4 pt = r.zero ? make_uint4(0, 0, 0, 0) : reinterpret_cast<const uint4*>(src)[w];
+        pt.x ^= ks[4 * w]; pt.y ^= ks[4 * w + 1]; pt.z ^= ks[4 * w + 2]; pt.w ^= ks[4 * w + 3];
+        reinterpret_cast<uint4*>(dst)[w] = pt;
+      }
+    } else {
+      xor_block_bytes(dst, src, ks, lo, hi);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// SipHash-2-4-128 chains: one lane per page
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t ld_u32_any(const uint8_t* p) {
+  return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+
+// Absorbs bytes [0, len) of p as little-endian words plus the length word (csrc:425-442) and
+// finalizes.  The 16-byte-aligned path keeps one 128-byte chunk in flight ahead of the chain.
+__device__ __forceinline__ void siphash_bytes(SipState& st, const uint8_t* p, int64_t len, uint32_t tag[4]) {
+  const int64_t n_words = len >> 3;
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+    const uint4* src = reinterpret_cast<const uint4*>(p);
+    const int64_t n_vec = n_words >> 1;
+    const int64_t n_chunks = n_vec >> 3;
+    uint4 cur[8];
+    if (n_chunks > 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cur[j] = __ldg(src + j);
+    }
+    for (int64_t c = 0; c < n_chunks; ++c) {
+      uint4 nxt[8];
+      const bool more = c + 1 < n_chunks;
+      if (more) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) nxt[j] = __ldg(src + (c + 1) * 8 + j);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        st.absorb(cur[j].x, cur[j].y);
+        st.absorb(cur[j].z, cur[j].w);
+      }
+      if (more) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+      }
+    }
+    for (int64_t i = n_chunks * 8; i < n_vec; ++i) {
+      const uint4 t = __ldg(src + i);
+      st.absorb(t.x, t.y);
+      st.absorb(t.z, t.w);
+    }
+    if (n_words & 1) {
+      const uint2 t = __ldg(reinterpret_cast<const uint2*>(p + (n_words - 1) * 8));
+      st.absorb(t.x, t.y);
+    }
+  } else {
+    for (int64_t i = 0; i < n_words; ++i) st.absorb(ld_u32_any(p + 8 * i), ld_u32_any(p + 8 * i + 4));
+  }
+  uint32_t lo = 0, hi = (uint32_t)(len & 0xff) << 24;
+  const int rem = (int)(len & 7);
+  const uint8_t* t = p + n_words * 8;
+  for (int b = 0; b < rem; ++b) {
+    if (b < 4) lo |= (uint32_t)t[b] << (8 * b);
+    else hi |= (uint32_t)t[b] << (8 * (b - 4));
+  }
+  st.absorb(lo, hi);
+  st.finish(tag);
+}
+
+template <bool VERIFY>
+__global__ void __launch_bounds__(128) mac_kernel(const __grid_constant__ MacParams P) {
+  const int64_t page = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (page >= P.n_pages) return;
+  uint8_t* blob = P.blobs + page * P.blob_stride;
+  const int64_t mac_len = kHeaderBytes + P.payload_len;
+  int32_t status = 0;
+  if (VERIFY) {
+    uint32_t h[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) h[i] = ld_u32_any(blob + 4 * i);
+    const uint64_t tok = ((uint64_t)h[5] << 32) | h[4];
+    if ((h[0] & 0xFFFFu) != kMagic || ((h[0] >> 16) & 0xFFu) != kVersion) status = 1;
+    else if (h[1] != P.meta.tenant || h[2] != P.meta.model || (h[3] & 0xFFFFu) != page_layer(P.meta, page) ||
+             tok != P.meta.token_hash[page])
+      status = 2;
+    if (status != 0) {
+      P.status[page] = status;
+      atomicOr(P.any_fail, 1);
+      return;
+    }
+  }
+  SipState st;
+  st.init(P.mk0, P.mk1);
+  uint32_t tag[4];
+  siphash_bytes(st, blob, mac_len, tag);
+  uint8_t* tag_ptr = blob + mac_len;
+  if (!VERIFY) {
+    if ((reinterpret_cast<uintptr_t>(tag_ptr) & 3) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) reinterpret_cast<uint32_t*>(tag_ptr)[i] = tag[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) tag_ptr[i] = (uint8_t)(tag[i >> 2] >> (8 * (i & 3)));
+    }
+    return;
+  }
+  uint32_t diff = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) diff |= tag[i] ^ ld_u32_any(tag_ptr + 4 * i);
+  if (diff != 0) {
+    status = 3;
+  } else {
+    const uint8_t flags = blob[3];
+    Layout L;
+    if (!build_layout(flags & 0x0F, (flags >> 4) & 0x0F, P.vecs, P.head_dim, P.rope_dim, P.has_v != 0, &L))
+      status = 4;
+    else if (P.payload_len < L.data_end)
+      status = 5;
+  }
+  P.status[page] = status;
+  if (status != 0) atomicOr(P.any_fail, 1);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Ingress: decrypt + dequantize one (page, vec-tile), or zero it when the batch failed
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kTileThreads) ingress_tile_kernel(const __grid_constant__ IngressParams P) {
+  extern __shared__ __align__(16) uint8_t stage[];
+  const int64_t page = blockIdx.x / P.n_tiles;
+  const int tile = (int)(blockIdx.x - page * P.n_tiles);
+  const int64_t v0 = (int64_t)tile * P.tile_vecs;
+  const int tv = (int)min((int64_t)P.tile_vecs, P.vecs - v0);
+  const int64_t blk = page_block(P.meta, page);
+  uint16_t* kd = P.k_out + blk * P.page_elems;
+  uint16_t* vd = P.v_out ? P.v_out + blk * P.page_elems : nullptr;
+
+  if (*P.any_fail != 0) {
+    const int64_t n16 = (int64_t)tv * P.head_dim / 8;  // uint4 per buffer
+    uint4* kz = reinterpret_cast<uint4*>(kd + v0 * P.head_dim);
+    uint4* vz = vd ? reinterpret_cast<uint4*>(vd + v0 * P.head_dim) : nullptr;
+    for (int64_t i = threadIdx.x; i < n16; i += blockDim.x) {
+      kz[i] = make_uint4(0, 0, 0, 0);
+      if (vz) vz[i] = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+
+  const uint8_t* blob = P.blobs + page * P.blob_stride;
+  const uint8_t flags = blob[3];
+  const uint32_t layer_hg = ld_u32_any(blob + 12);
+  const uint64_t seq = ((uint64_t)ld_u32_any(blob + 28) << 32) | ld_u32_any(blob + 24);
+  Layout L;
+  build_layout(flags & 0x0F, (flags >> 4) & 0x0F, P.vecs, P.head_dim, P.rope_dim, P.has_v != 0, &L);
+  int32_t sq[3], ss[3];
+  plan_stage(L, P.tile_vecs, sq, ss);
+
+  // ---- phase 1: decrypt this tile's byte ranges into shared memory
+  Range R[7];
+  const int nr = tile_ranges(L, v0, tv, sq, ss, false, P.payload_len, R);
+  int64_t nb[7];
+  int64_t total_blocks = 0;
+#pragma unroll
+  for (int i = 0; i < 7; ++i) {
+    nb[i] = i < nr ? range_blocks(R[i]) : 0;
+    total_blocks += nb[i];
+  }
+  const uint32_t n2 = (layer_hg << 16) | (layer_hg >> 16);  // layer_id << 16 | head_group_id
+  const uint8_t* payload = blob + kHeaderBytes;
+  for (int64_t bi = threadIdx.x; bi < total_blocks; bi += blockDim.x) {
+    int i = 0;
+    int64_t local = bi;
+    while (i < nr - 1 && local >= nb[i]) { local -= nb[i]; ++i; }
+    const Range r = R[i];
+    const int64_t kb = (r.a >> 6) + local;
+    uint32_t ks[16];
+    chacha20_block(P.key, (uint32_t)(1 + kb), (uint32_t)seq, (uint32_t)(seq >> 32), n2, ks);
+    const int64_t base = kb << 6;
+    const int lo = (int)(max(r.a, base) - base), hi = (int)(min(r.b, base + 64) - base);
+    const uint8_t* src = payload + base;
+    uint8_t* dst = stage + r.stage + (base - r.a);  // only bytes [lo, hi) are written
+    if (lo == 0 && hi == 64 &&
+        ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint4 c = __ldg(reinterpret_cast<const uint4*>(src) + w);
+        c.x ^= ks[4 * w]; c.y ^= ks[4 * w + 1]; c.z ^= ks[4 * w + 2]; c.w ^= ks[4 * w + 3];
+        reinterpret_cast<uint4*>(dst)[w] = c;
+      }
+    } else {
+#pragma unroll
+      for (int w = 0; w < 16; ++w) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int x = 4 * w + j;
+          if (x >= lo && x < hi) dst[x] = (uint8_t)(src[x] ^ (uint8_t)(ks[w] >> (8 * j)));
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 2: dequantize into the paged KV layout
+  int items[3] = {0, 0, 0};
+  int total = 0;
+#pragma unroll
+  for (int s = 0; s < 3; ++s)
+    if (s < L.n) {
+      items[s] = tv * (pick(L, s).dim >> 4);
+      total += items[s];
+    }
+  for (int it = threadIdx.x; it < total; it += blockDim.x) {
+    int s = 0, local = it;
+    if (local >= items[0]) { local -= items[0]; s = 1; if (local >= items[1]) { local -= items[1]; s = 2; } }
+    const Section S = pick(L, s);
+    const int groups = S.dim >> 4;
+    const int vec = local / groups, g = local - vec * groups;
+    uint4* dst = reinterpret_cast<uint4*>((S.buf ? vd : kd) + (v0 + vec) * P.head_dim + S.col + g * 16);
+    const uint8_t* qs = stage + (s == 0 ? sq[0] : (s == 1 ? sq[1] : sq[2])) + vec * S.q_bpv;
+    const uint8_t* sc = stage + (s == 0 ? ss[0] : (s == 1 ? ss[1] : ss[2])) + vec * S.s_bpv + g * 2;
+    uint32_t o[8];
+    if (S.kind == kRaw) {
+      const uint4* q = reinterpret_cast<const uint4*>(qs + g * 32);
+      dst[0] = q[0];
+      dst[1] = q[1];
+      continue;
+    } else if (S.kind == kInt8) {
+      const uint4 q = *reinterpret_cast<const uint4*>(qs + g * 16);
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+      dequant_int8(qw, *reinterpret_cast<const uint16_t*>(sc), o);
+    } else {
+      const uint2 q = *reinterpret_cast<const uint2*>(qs + g * 8);
+      const uint32_t qw[2] = {q.x, q.y};
+      dequant_int4(qw, *reinterpret_cast<const uint16_t*>(sc), o);
+    }
+    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Known-answer entry points (csrc:2499-2538)
+// ------------------------------------------------------------------------------------------------
+__global__ void chacha20_xor_kernel(const uint8_t* src, uint8_t* dst, int64_t len, const uint32_t k0, uint32_t k1,
+                                    uint32_t k2, uint32_t k3, uint32_t k4, uint32_t k5, uint32_t k6, uint32_t k7,
+                                    uint32_t counter0, uint32_t n0, uint32_t n1, uint32_t n2) {
+  const int64_t kb = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (kb * 64 >= len) return;
+  const uint32_t key[8] = {k0, k1, k2, k3, k4, k5, k6, k7};
+  uint32_t ks[16];
+  chacha20_block(key, counter0 + (uint32_t)kb, n0, n1, n2, ks);
+  const int hi = (int)min((int64_t)64, len - kb * 64);
+  const uint8_t* s = src + kb * 64;
+  uint8_t* d = dst + kb * 64;
+#pragma unroll
+  for (int w = 0; w < 16; ++w) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int x = 4 * w + j;
+      if (x < hi) d[x] = (uint8_t)(s[x] ^ (uint8_t)(ks[w] >> (8 * j)));
+    }
+  }
+}
+
+__global__ void siphash_kernel(const uint8_t* src, int64_t len, uint64_t k0, uint64_t k1, uint8_t* out16) {
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  SipState st;
+  st.init(k0, k1);
+  uint32_t tag[4];
+  siphash_bytes(st, src, len, tag);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) out16[i] = (uint8_t)(tag[i >> 2] >> (8 * (i & 3)));
+}
+
+template <typename K>
+void ensure_smem(K kernel, int32_t bytes) {
+  if (bytes > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+}  // namespace
+
+void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream) {
+  const int64_t grid = P.n_pages * P.n_tiles;
+  if (bf16) {
+    ensure_smem(egress_tile_kernel<true>, P.stage_bytes);
+    egress_tile_kernel<true><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+  } else {
+    ensure_smem(egress_tile_kernel<false>, P.stage_bytes);
+    egress_tile_kernel<false><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+  }
+}
+
+void launch_mac(const MacParams& P, bool verify, cudaStream_t stream) {
+  const unsigned grid = (unsigned)((P.n_pages + 127) / 128);
+  if (verify) mac_kernel<true><<<grid, 128, 0, stream>>>(P);
+  else mac_kernel<false><<<grid, 128, 0, stream>>>(P);
+}
+
+void launch_ingress(const IngressParams& P, cudaStream_t stream) {
+  const int64_t grid = P.n_pages * P.n_tiles;
+  ensure_smem(ingress_tile_kernel, P.stage_bytes);
+  ingress_tile_kernel<<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+}
+
+void launch_chacha20_xor(const uint8_t* src, uint8_t* dst, int64_t len, const uint32_t key[8], uint32_t counter0,
+                         const uint32_t nonce[3], cudaStream_t stream) {
+  const int64_t blocks = (len + 63) / 64;
+  const unsigned grid = (unsigned)((blocks + 127) / 128);
+  chacha20_xor_kernel<<<grid, 128, 0, stream>>>(src, dst, len, key[0], key[1], key[2], key[3], key[4], key[5],
+                                                key[6], key[7], counter0, nonce[0], nonce[1], nonce[2]);
+}
+
+void launch_siphash(const uint8_t* src, int64_t len, uint64_t k0, uint64_t k1, uint8_t* out16, cudaStream_t stream) {
+  siphash_kernel<<<1, 32, 0, stream>>>(src, len, k0, k1, out16);
+}
+
+}  // namespace ztcp

@@ -1,0 +1,103 @@
+// ztcp_kernels.cuh -- kernel parameter blocks shared by the kernels and the host launchers.
+#pragma once
+#include <stdint.h>
+
+#include "ztcp_layout.h"
+
+namespace ztcp {
+
+// Per-page metadata of a batch.  Device pointers may be null: kv_block -> identity, sequence_nonce ->
+// seq_base + page index (the reference's batch rule, csrc:1994), layer_id -> layer_uniform.
+struct PageMeta {
+  const int32_t* kv_block;
+  const uint64_t* token_hash;
+  const uint64_t* sequence_nonce;
+  const uint16_t* layer_id;
+  uint64_t seq_base;
+  uint32_t tenant;
+  uint32_t model;
+  uint16_t layer_uniform;
+  uint16_t head_group;
+};
+
+constexpr int kTileThreads = 256;
+
+struct EgressParams {
+  const uint16_t* k;        // KV pool (fp16 or bf16 bits), page p at k + kv_block[p] * page_elems
+  const uint16_t* v;        // null for a single-buffer MLA page
+  int64_t page_elems;
+  uint8_t* out;             // blobs, page p at out + p * blob_stride
+  int64_t blob_stride;
+  int64_t payload_len;
+  int64_t vecs;
+  int32_t head_dim;
+  int32_t flags;            // header flags byte
+  Layout L;
+  PageMeta meta;
+  uint32_t key[8];
+  int32_t tile_vecs;
+  int32_t n_tiles;
+  int64_t n_pages;
+  int32_t stage_q[3];       // shared-memory staging offsets (bytes) for a full tile
+  int32_t stage_s[3];
+  int32_t stage_bytes;
+};
+
+struct MacParams {
+  uint8_t* blobs;           // written (tag) in sign mode, read-only in verify mode
+  int64_t blob_stride;
+  int64_t payload_len;
+  int64_t n_pages;
+  uint64_t mk0, mk1;
+  // verify mode only
+  PageMeta meta;
+  int64_t vecs;
+  int64_t head_dim;
+  int64_t rope_dim;
+  int32_t has_v;
+  int32_t* status;          // [n_pages]
+  int32_t* any_fail;        // [1], zeroed by the launcher
+};
+
+struct IngressParams {
+  const uint8_t* blobs;
+  int64_t blob_stride;
+  int64_t payload_len;
+  uint16_t* k_out;          // fp16 outputs, page p at k_out + kv_block[p] * page_elems
+  uint16_t* v_out;
+  int64_t page_elems;
+  int64_t vecs;
+  int32_t head_dim;
+  int32_t rope_dim;
+  int32_t has_v;
+  PageMeta meta;
+  uint32_t key[8];
+  const int32_t* any_fail;
+  int32_t tile_vecs;
+  int32_t n_tiles;
+  int64_t n_pages;
+  int32_t stage_bytes;
+};
+
+void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream);
+void launch_mac(const MacParams& P, bool verify, cudaStream_t stream);
+void launch_ingress(const IngressParams& P, cudaStream_t stream);
+void launch_chacha20_xor(const uint8_t* src, uint8_t* dst, int64_t len, const uint32_t key[8], uint32_t counter0,
+                         const uint32_t nonce[3], cudaStream_t stream);
+void launch_siphash(const uint8_t* src, int64_t len, uint64_t k0, uint64_t k1, uint8_t* out16, cudaStream_t stream);
+
+// Staging layout of one tile: 16-byte aligned q and scale areas per section.
+ZTCP_HD int32_t plan_stage(const Layout& L, int32_t tile_vecs, int32_t stage_q[3], int32_t stage_s[3]) {
+  int64_t off = 0;
+  for (int i = 0; i < 3; ++i) {
+    stage_q[i] = stage_s[i] = 0;
+    if (i >= L.n) continue;
+    stage_q[i] = (int32_t)off;
+    off += ((int64_t)tile_vecs * L.sec[i].q_bpv + 15) / 16 * 16;
+    stage_s[i] = (int32_t)off;
+    off += ((int64_t)tile_vecs * L.sec[i].s_bpv + 15) / 16 * 16;
+  }
+  return (int32_t)off;
+}
+
+}  // namespace ztcp

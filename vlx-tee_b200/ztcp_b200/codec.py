@@ -1,0 +1,188 @@
+"""GPU-native batch API over the C-ABI: block tables and per-page metadata.
+
+``encode_pages`` / ``decode_pages`` take CUDA tensors that already live on
+one device and enqueue the kernels on the current torch stream without
+synchronizing.  They are the building blocks of the reference-compatible
+module in ``fused_ext`` and of the benchmark.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import capi
+
+_U64 = (1 << 64) - 1
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(name: str, t: torch.Tensor, dtypes, device: torch.device | None = None) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise RuntimeError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise RuntimeError(f"{name} must be a CUDA tensor")
+    if device is not None and t.device != device:
+        raise RuntimeError(f"{name} must be on {device}, got {t.device}")
+    if not t.is_contiguous():
+        raise RuntimeError(f"{name} must be contiguous")
+    if t.dtype not in dtypes:
+        raise RuntimeError(f"{name} must have dtype in {[str(d) for d in dtypes]}, got {t.dtype}")
+
+
+def _page_batch(n_pages: int, token_hashes: torch.Tensor, block_table, sequence_nonces, layer_ids,
+                base_sequence_nonce: int, tenant: int, model: int, layer_id: int, head_group: int) -> capi.PageBatch:
+    b = capi.PageBatch()
+    b.n_pages = n_pages
+    b.kv_block = _ptr(block_table)
+    b.token_hash = _ptr(token_hashes)
+    b.sequence_nonce = _ptr(sequence_nonces)
+    b.layer_id = _ptr(layer_ids)
+    b.base_sequence_nonce = int(base_sequence_nonce) & _U64
+    b.tenant_id_hash = int(tenant) & 0xFFFFFFFF
+    b.model_id_hash = int(model) & 0xFFFFFFFF
+    b.layer_id_uniform = int(layer_id) & 0xFFFF
+    b.head_group_id = int(head_group) & 0xFFFF
+    return b
+
+
+def _check_meta(dev, n, block_table, sequence_nonces, layer_ids, token_hashes):
+    _require_cuda("page_token_hashes", token_hashes, (torch.int64, torch.uint64), dev)
+    if token_hashes.dim() != 1 or token_hashes.numel() != n:
+        raise RuntimeError("page_token_hashes must be 1D with length equal to batch_size")
+    if block_table is not None:
+        _require_cuda("block_table", block_table, (torch.int32,), dev)
+        if block_table.dim() != 1 or block_table.numel() != n:
+            raise RuntimeError("block_table must be 1D int32 with one entry per page")
+    if sequence_nonces is not None:
+        _require_cuda("sequence_nonces", sequence_nonces, (torch.int64, torch.uint64), dev)
+        if sequence_nonces.dim() != 1 or sequence_nonces.numel() != n:
+            raise RuntimeError("sequence_nonces must be 1D with one entry per page")
+    if layer_ids is not None:
+        _require_cuda("layer_ids", layer_ids, (torch.int16, torch.uint16), dev)
+        if layer_ids.dim() != 1 or layer_ids.numel() != n:
+            raise RuntimeError("layer_ids must be 1D int16 with one entry per page")
+
+
+def _check_block_table(block_table: torch.Tensor | None, pool_pages: int) -> None:
+    # kv_block entries index the pool; a bad entry would address memory outside it.
+    if block_table is not None and block_table.numel() > 0:
+        lo, hi = torch.aminmax(block_table)
+        if int(lo) < 0 or int(hi) >= pool_pages:
+            raise RuntimeError(f"block_table entries must lie in [0, {pool_pages})")
+
+
+def encode_pages(k_pool: torch.Tensor, v_pool: torch.Tensor | None, token_hashes: torch.Tensor,
+                 out_blobs: torch.Tensor, *, rope_dim: int, preset: int, rope_mode: int, expected_payload_bytes: int,
+                 tenant_id_hash: int, model_id_hash: int, layer_id: int, head_group_id: int,
+                 base_sequence_nonce: int, keys: capi.Keys, block_table: torch.Tensor | None = None,
+                 sequence_nonces: torch.Tensor | None = None, layer_ids: torch.Tensor | None = None,
+                 check_block_table: bool = True) -> None:
+    """Egress of ``out_blobs.shape[0]`` pages from a KV pool [pool_pages, T, H, D] (fp16 or bf16).
+
+    Page i reads pool block ``block_table[i]`` (default i) and is written to out_blobs[i].
+    """
+    dev = k_pool.device
+    _require_cuda("k_pages", k_pool, (torch.float16, torch.bfloat16))
+    if k_pool.dim() != 4:
+        raise RuntimeError("k_pages must have shape [batch, num_tokens, num_heads, head_dim]")
+    if v_pool is not None:
+        _require_cuda("v_pages", v_pool, (k_pool.dtype,), dev)
+        if v_pool.shape != k_pool.shape:
+            raise RuntimeError("v_pages shape must match k_pages shape")
+    _require_cuda("out_blobs", out_blobs, (torch.uint8,), dev)
+    if out_blobs.dim() != 2:
+        raise RuntimeError("out_blobs must have shape [batch, total_blob_bytes]")
+    n = out_blobs.shape[0]
+    if out_blobs.shape[1] != 32 + expected_payload_bytes + 16:
+        raise RuntimeError("out_blobs shape must be [batch_size, total_blob_bytes]")
+    if block_table is None and n != k_pool.shape[0]:
+        raise RuntimeError("out_blobs batch size must match k_pages batch size")
+    _check_meta(dev, n, block_table, sequence_nonces, layer_ids, token_hashes)
+    if check_block_table:
+        _check_block_table(block_table, k_pool.shape[0])
+    _, T, H, D = k_pool.shape
+    geom = capi.geometry(T, H, D, rope_dim, v_pool is None)
+    batch = _page_batch(n, token_hashes, block_table, sequence_nonces, layer_ids, base_sequence_nonce,
+                        tenant_id_hash, model_id_hash, layer_id, head_group_id)
+    dtype = capi.DTYPE_BF16 if k_pool.dtype == torch.bfloat16 else capi.DTYPE_F16
+    lib = capi.load()
+    with torch.cuda.device(dev):
+        rc = lib.ztcp_encode_pages(_ptr(k_pool), _ptr(v_pool), dtype, geom, batch, int(preset), int(rope_mode),
+                                   int(expected_payload_bytes), keys, _ptr(out_blobs), _stream_handle(dev))
+    capi.check(rc)
+
+
+def decode_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, out_k: torch.Tensor,
+                 out_v: torch.Tensor | None, *, rope_dim: int, is_mla: bool, tenant_id_hash: int,
+                 model_id_hash: int, layer_id: int, keys: capi.Keys, block_table: torch.Tensor | None = None,
+                 layer_ids: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                 any_fail: torch.Tensor | None = None, check_block_table: bool = True):
+    """Ingress of ``blobs.shape[0]`` pages into fp16 pools [pool_pages, T, H, D].
+
+    Enqueues verify + decrypt; returns the device tensors (status[n] int32, any_fail[1] int32).  When
+    any page fails, every output page of the batch is zeroed.
+    """
+    dev = blobs.device
+    _require_cuda("cold_blobs", blobs, (torch.uint8,))
+    if blobs.dim() != 2:
+        raise RuntimeError("cold_blobs must have shape [batch, total_blob_bytes]")
+    n, blob_bytes = blobs.shape
+    _require_cuda("out_k_pages", out_k, (torch.float16,), dev)
+    if out_k.dim() != 4:
+        raise RuntimeError("out_k_pages must have shape [batch, num_tokens, num_heads, head_dim]")
+    if out_v is not None:
+        _require_cuda("out_v_pages", out_v, (torch.float16,), dev)
+        if out_v.shape != out_k.shape:
+            raise RuntimeError("out_v_pages shape must match out_k_pages shape")
+    if block_table is None and n != out_k.shape[0]:
+        raise RuntimeError("cold_blobs batch size must match out_k_pages batch size")
+    _check_meta(dev, n, block_table, None, layer_ids, token_hashes)
+    if check_block_table:
+        _check_block_table(block_table, out_k.shape[0])
+    if status is None:
+        status = torch.empty(n, dtype=torch.int32, device=dev)
+    if any_fail is None:
+        any_fail = torch.empty(1, dtype=torch.int32, device=dev)
+    _, T, H, D = out_k.shape
+    geom = capi.geometry(T, H, D, rope_dim, is_mla)
+    batch = _page_batch(n, token_hashes, block_table, None, layer_ids, 0, tenant_id_hash, model_id_hash,
+                        layer_id, 0)
+    lib = capi.load()
+    with torch.cuda.device(dev):
+        rc = lib.ztcp_decode_pages(_ptr(blobs), int(blob_bytes), geom, batch, keys, _ptr(out_k), _ptr(out_v),
+                                   _ptr(status), _ptr(any_fail), _stream_handle(dev))
+    capi.check(rc)
+    return status, any_fail
+
+
+# Exception texts of the reference's batch and single-page decoders (csrc:2236-2244, :1582-1637).
+BATCH_MESSAGES = {
+    capi.PAGE_BAD_MAGIC: "KV_INTEGRITY_ERROR: Invalid cold-page header magic, version, or flags",
+    capi.PAGE_BAD_FLAGS: "KV_INTEGRITY_ERROR: Invalid cold-page header magic, version, or flags",
+    capi.PAGE_TRUNCATED: "KV_INTEGRITY_ERROR: Invalid cold-page header magic, version, or flags",
+    capi.PAGE_AAD_MISMATCH: "CROSS_TENANT_CONTAMINATION: Cold-page AAD mismatch",
+    capi.PAGE_MAC_FAILED: "KV_INTEGRITY_ERROR: Cold-page MAC verification failed",
+}
+SINGLE_MESSAGES = {
+    capi.PAGE_BAD_MAGIC: "KV_INTEGRITY_ERROR: Invalid cold-page header magic or version",
+    capi.PAGE_AAD_MISMATCH: "CROSS_TENANT_CONTAMINATION: Cold-page AAD mismatch",
+    capi.PAGE_MAC_FAILED: "KV_INTEGRITY_ERROR: Cold-page MAC verification failed",
+    capi.PAGE_BAD_FLAGS: "KV_INTEGRITY_ERROR: Invalid cold-page header flags (preset or rope_mode)",
+    capi.PAGE_TRUNCATED: "KV_INTEGRITY_ERROR: Cold-page payload truncated for header flags",
+}
+
+
+def raise_for_status(status: torch.Tensor, any_fail: torch.Tensor, single: bool = False) -> None:
+    """Synchronize on the decode and raise the reference's error for the first failing page."""
+    if int(any_fail.item()) == 0:
+        return
+    st = status.cpu()
+    bad = torch.nonzero(st != 0)
+    code = int(st[int(bad[0])]) if bad.numel() else capi.PAGE_MAC_FAILED
+    raise RuntimeError((SINGLE_MESSAGES if single else BATCH_MESSAGES)[code])
