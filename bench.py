@@ -1,0 +1,404 @@
+#!/usr/bin/env python
+"""ZTCP cold-page codec benchmark on B200 -- prints one JSON line (rank 0).
+
+Workload: BASELINE configuration 0 -- a batch of 256 GQA pages (64 tokens x 8 KV heads x 128, separate
+K and V in bf16, 256 KiB hot per page), INT4_SYM + PRESERVE_FP8, N(0,1) values with four x15 RoPE
+outlier channels per head, random 256-bit ChaCha20 key, 128-bit SipHash key and 64-bit base nonce.
+One step = egress (quantize, pack, encrypt, tag) of the batch followed by ingress (verify, decrypt,
+dequantize) of the blobs it produced.  value = (egress + ingress) hot bytes / time, SI GB/s.
+
+Multi-GPU: pages are independent, so every rank encodes and decodes its own 256-page batch with no
+collective on the data path (weak scaling); the only collectives are the barrier and the max-over-ranks
+reduction of the timings.
+
+--impl reference times the reference codec (built from its own source into oracle/_ref) on the host
+cores: one process per core, each running the reference's peak egress and peak ingress entry points on
+its share of pages.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(REPO, "vlx-tee_b200"))
+
+PAGE_HOT_BYTES = 2 * 64 * 8 * 128 * 2       # K + V, bf16/fp16
+EXPECTED_PAYLOAD = 98304                     # INT4_SYM + PRESERVE_FP8, GQA 64x8x128
+BLOB_BYTES = 32 + EXPECTED_PAYLOAD + 16
+CHACHA_BLOCKS_PER_PAGE = EXPECTED_PAYLOAD // 64
+SIP_WORDS_PER_PAGE = (32 + EXPECTED_PAYLOAD) // 8 + 1
+METRIC = "egress+ingress hot-byte GB/s (INT4_SYM+PRESERVE_FP8 256-page GQA batch)"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--pages", type=int, default=256, help="pages per GPU per step")
+    ap.add_argument("--sets", type=int, default=4, help="rotating input sets (working set > L2)")
+    ap.add_argument("--e2e-steps", type=int, default=6)
+    ap.add_argument("--cpu-seconds", type=float, default=8.0, help="bounded CPU baseline sample length")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+def committed_traffic():
+    """Per-launch DRAM traffic of the dominant kernel from the committed ncu summary, if any."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+# ------------------------------------------------------------------------------------------------
+# clocks during the timed region
+# ------------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id: str | None):
+        self.bus_id = bus_id
+        self.proc = None
+        self.path = os.path.join("/tmp", f"ztcp_clocks_{os.getpid()}.csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 10:
+                    continue
+                if self.bus_id and parts[1].upper() != self.bus_id.upper():
+                    continue
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[6:10]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][3]),
+                "reasons": reasons, "samples": len(rows)}
+
+
+def bus_id_of(dev_index: int) -> str | None:
+    import torch
+
+    p = torch.cuda.get_device_properties(dev_index)
+    try:
+        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
+    except AttributeError:
+        return None
+
+
+# ------------------------------------------------------------------------------------------------
+# reference codec on the host cores
+# ------------------------------------------------------------------------------------------------
+def _ref_worker(args):
+    """One process: the reference's peak egress + peak ingress on `pages` pages until `seconds` pass."""
+    worker, pages, seconds = args
+    sys.path.insert(0, os.path.join(REPO, "oracle"))
+    sys.path.insert(0, os.path.join(REPO, "vlx-tee_b200"))
+    import torch
+
+    import build_ref
+    from ztcp_b200 import workload
+
+    torch.set_num_threads(1)
+    ref = build_ref.load_module()
+    k32, v32 = workload.kv_pages_np(pages, workload.GQA, seed=42 + worker)
+    k = torch.from_numpy(k32).to(torch.bfloat16).half()   # the reference codec accepts fp16 only
+    v = torch.from_numpy(v32).to(torch.bfloat16).half()
+    m = workload.session_material(7)
+    toks = torch.from_numpy(workload.token_hashes(pages, 11 + worker))
+    out = torch.empty((pages, BLOB_BYTES), dtype=torch.uint8)
+    kd, vd = torch.empty_like(k), torch.empty_like(v)
+    key, mk = m["key"], m["mac_key"]
+    done, it = 0, 0
+    t0 = time.perf_counter()
+    while True:
+        ref.fused_encode_cold_pages_peak_into_cpu(k, v, toks, out, 1, 1, 64, EXPECTED_PAYLOAD, m["tenant"],
+                                                  m["model"], m["layer"], m["head_group"],
+                                                  (m["base_seq"] + it * pages + worker * 2**32) % 2**64,
+                                                  key[0], key[1], mk[0], mk[1], key[2], key[3])
+        ref.fused_decode_cold_pages_peak_into_cpu(out, toks, kd, vd, 64, False, m["tenant"], m["model"], m["layer"],
+                                                  key[0], key[1], mk[0], mk[1], key[2], key[3])
+        done += pages
+        it += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            return done, el
+
+
+def reference_baseline(seconds: float, pages_per_worker: int = 8):
+    import multiprocessing as mp
+
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        res = pool.map(_ref_worker, [(w, pages_per_worker, seconds) for w in range(cores)])
+    pages = sum(r[0] for r in res)
+    wall = max(r[1] for r in res)
+    gbs = 2 * pages * PAGE_HOT_BYTES / wall / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
+            "sample": (f"{cores} processes x {pages_per_worker}-page batches for {seconds:.0f} s: reference "
+                       f"fused_encode_cold_pages_peak_into_cpu + fused_decode_cold_pages_peak_into_cpu "
+                       f"(oracle/_ref, scalar x86-64 build, 1 thread each); {pages} pages round-tripped")}
+
+
+def reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    base = reference_baseline(args.cpu_seconds)
+    per_step_ms = 2 * args.pages * PAGE_HOT_BYTES / (base["value"] * 1e9) * 1e3
+    line = {"metric": METRIC, "value": base["value"], "unit": "GB/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "config": {"workload": "cfg0: 256-page GQA 64x8x128 INT4_SYM+PRESERVE_FP8 egress+ingress",
+                       "pages": args.pages, "host_cores": base["cores"]},
+            "cpu_baseline": base,
+            "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+
+
+# ------------------------------------------------------------------------------------------------
+# our arm
+# ------------------------------------------------------------------------------------------------
+def ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from ztcp_b200 import capi, codec, fused_ext, workload
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    # baseline sample first: the spawn pool starts before this process does GPU work
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu_base = reference_baseline(args.cpu_seconds)
+
+    n = args.pages
+    m = workload.session_material(7)
+    keys = capi.keys(*m["key"], *m["mac_key"])
+    sets = []
+    for s in range(args.sets):
+        seed = 42 + 1000 * rank + s
+        k, v = workload.kv_pages_torch(n, workload.GQA, seed=seed, device=dev)
+        toks = torch.from_numpy(workload.token_hashes(n, seed)).to(dev)
+        sets.append({
+            "k": k, "v": v, "toks": toks,
+            "seq": (m["base_seq"] + (rank * args.sets + s) * n) % 2**64,
+            "blobs": torch.empty((n, BLOB_BYTES), dtype=torch.uint8, device=dev),
+            "kout": torch.empty((n, 64, 8, 128), dtype=torch.float16, device=dev),
+            "vout": torch.empty((n, 64, 8, 128), dtype=torch.float16, device=dev),
+            "status": torch.empty(n, dtype=torch.int32, device=dev),
+            "fail": torch.zeros(1, dtype=torch.int32, device=dev),
+        })
+
+    def egress(S):
+        codec.encode_pages(S["k"], S["v"], S["toks"], S["blobs"], rope_dim=64, preset=1, rope_mode=1,
+                           expected_payload_bytes=EXPECTED_PAYLOAD, tenant_id_hash=m["tenant"],
+                           model_id_hash=m["model"], layer_id=m["layer"], head_group_id=m["head_group"],
+                           base_sequence_nonce=S["seq"], keys=keys)
+
+    def ingress(S):
+        codec.decode_pages(S["blobs"], S["toks"], S["kout"], S["vout"], rope_dim=64, is_mla=False,
+                           tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"], keys=keys,
+                           status=S["status"], any_fail=S["fail"])
+
+    def verify(S):
+        codec.verify_pages(S["blobs"], S["toks"], num_tokens=64, num_heads=8, head_dim=128, rope_dim=64,
+                           is_mla=False, tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"],
+                           keys=keys, status=S["status"], any_fail=S["fail"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for i in range(args.warmup):
+        S = sets[i % len(sets)]
+        egress(S)
+        ingress(S)
+    torch.cuda.synchronize()
+    for S in sets:
+        if int(S["fail"].item()) != 0:
+            raise RuntimeError("warm-up round trip failed verification")
+
+    K = args.steps
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
+    with ClockSampler(bus_id_of(local)) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        for i in range(K):
+            S = sets[i % len(sets)]
+            ev[i][0].record()
+            egress(S)
+            ev[i][1].record()
+            ingress(S)
+            ev[i][2].record()
+        torch.cuda.synchronize()
+        barrier()
+    total_ms = ev[0][0].elapsed_time(ev[-1][2])
+    egress_ms = sum(e[0].elapsed_time(e[1]) for e in ev)
+    ingress_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
+    bad = sum(int(S["fail"].item()) for S in sets)
+    if bad:
+        raise RuntimeError("a timed round trip failed verification")
+
+    # dominant kernel (SipHash chain): verify-only launches, timed live with events
+    mac_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
+    for i in range(K):
+        S = sets[i % len(sets)]
+        mac_ev[i][0].record()
+        verify(S)
+        mac_ev[i][1].record()
+    torch.cuda.synchronize()
+    mac_ms = statistics.mean(a.elapsed_time(b) for a, b in mac_ev)
+
+    t = torch.tensor([total_ms, egress_ms, ingress_ms, mac_ms], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, egress_ms, ingress_ms, mac_ms = (float(x) for x in t.tolist())
+
+    # end to end through the drop-in API with pinned host buffers (the reference wrapper's placement)
+    S0 = sets[0]
+    hk, hv = S0["k"].cpu().pin_memory(), S0["v"].cpu().pin_memory()
+    htoks = S0["toks"].cpu()
+    hblobs = torch.empty((n, BLOB_BYTES), dtype=torch.uint8).pin_memory()
+    hko = torch.empty((n, 64, 8, 128), dtype=torch.float16).pin_memory()
+    hvo = torch.empty_like(hko).pin_memory()
+
+    def e2e_step(i):
+        fused_ext.fused_encode_cold_pages_peak_into_cpu(
+            hk, hv, htoks, hblobs, 1, 1, 64, EXPECTED_PAYLOAD, m["tenant"], m["model"], m["layer"],
+            m["head_group"], (S0["seq"] + (i + 1) * 2**40) % 2**64, m["key"][0], m["key"][1], m["mac_key"][0],
+            m["mac_key"][1], m["key"][2], m["key"][3])
+        fused_ext.fused_decode_cold_pages_peak_into_cpu(
+            hblobs, htoks, hko, hvo, 64, False, m["tenant"], m["model"], m["layer"], m["key"][0], m["key"][1],
+            m["mac_key"][0], m["mac_key"][1], m["key"][2], m["key"][3])
+
+    for i in range(2):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(args.e2e_steps):
+        e2e_step(i + 2)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+        barrier()
+    e2e_ms = float(e2e_ms.item())
+
+    if rank == 0:
+        hot_step = 2 * n * PAGE_HOT_BYTES * world
+        wire_step = 2 * n * BLOB_BYTES * world
+        value = hot_step / (total_ms / K * 1e-3) / 1e9
+        peak, peak_kind = measured_peaks()
+        mac_bytes = n * BLOB_BYTES
+        achieved = mac_bytes / (mac_ms * 1e-3) / 1e9
+        traffic = committed_traffic().get("mac_kernel<verify>", {}).get("dram_bytes_per_launch")
+        step_bytes = n * (PAGE_HOT_BYTES + BLOB_BYTES) * 2      # read+write, egress+ingress, one GPU
+        sm_mhz = clocks.summary()
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / K, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, int4/int8 + fp16 scales, fp16 out",
+            "data": "synthetic (seeded N(0,1), x15 RoPE outlier channels)",
+            "config": {"workload": "cfg0: 256-page GQA 64x8x128 INT4_SYM+PRESERVE_FP8 egress+ingress round trip",
+                       "pages_per_gpu": n, "parallelism": f"pages sharded, {world} GPU(s), no collective",
+                       "l2": f"{args.sets} rotating input sets, {args.sets * n * (PAGE_HOT_BYTES * 2 + BLOB_BYTES) / 1e6:.0f} MB working set > 126 MB L2"},
+            "egress_gbs": round(n * world * PAGE_HOT_BYTES / (egress_ms / K * 1e-3) / 1e9, 2),
+            "ingress_gbs": round(n * world * PAGE_HOT_BYTES / (ingress_ms / K * 1e-3) / 1e9, 2),
+            "wire_gbs": round(wire_step / (total_ms / K * 1e-3) / 1e9, 2),
+            "latency_ms": {"egress": round(egress_ms / K, 4), "ingress": round(ingress_ms / K, 4)},
+            "roofline": {"kernel": "mac_kernel<verify> (SipHash-2-4-128 chain, one lane per page)", "bound": "hbm",
+                         "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 5), "traffic": traffic,
+                         "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
+                         "algorithmic_bytes_per_launch": mac_bytes, "launch_ms": round(mac_ms, 4)},
+            "path_bounds_ms": {
+                "hbm": round(step_bytes / (peak * 1e9) * 1e3, 4),
+                "chacha20_alu": round(2 * n * CHACHA_BLOCKS_PER_PAGE / 28.5e9 * 1e3, 4),
+                "siphash_alu": round(2 * n * SIP_WORDS_PER_PAGE / 410e9 * 1e3, 4),
+                "siphash_chain": round(2 * SIP_WORDS_PER_PAGE * 89.3 / ((sm_mhz.get("sm_mhz") or 1965) * 1e6) * 1e3, 4),
+                "note": "chacha20 28.5 G blocks/s, siphash 410 G words/s at full occupancy and 89.3 cycles/word per "
+                        "chain are microbenchmarked (profiles/int_alu_peaks.md)"},
+            "clocks": sm_mhz,
+            "e2e": {"value": round(hot_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": n * (PAGE_HOT_BYTES + BLOB_BYTES + 8 * 2),
+                    "d2h_bytes_per_step": n * (BLOB_BYTES + PAGE_HOT_BYTES),
+                    "path": "ztcp_b200.fused_ext peak_into egress + ingress, pinned host K/V/blobs, "
+                            "synchronous like the reference"},
+            "gpu_launches": 4 * K,
+        }
+        if cpu_base is not None:
+            line["cpu_baseline"] = cpu_base
+        print(json.dumps(line))
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -122,6 +122,13 @@ int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_g
                           const ztcp_page_batch* batch, const ztcp_keys* keys, uint16_t* out_k, uint16_t* out_v,
                           int32_t* status, int32_t* any_fail, void* stream);
 
+/* Integrity check only: the checks of ztcp_decode_pages (magic/version, AAD, SipHash tag, flags,
+ * length) without decrypting -- status[i] and *any_fail as ztcp_decode_pages writes them.  Replaces
+ * the verification steps of the reference's decoders (csrc:2312-2355) for scrubbing stored blobs. */
+int32_t ztcp_verify_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_geometry* geom,
+                          const ztcp_page_batch* batch, const ztcp_keys* keys, int32_t* status, int32_t* any_fail,
+                          void* stream);
+
 /* RFC 8439 ChaCha20 keystream XOR of `len` device bytes (src may equal dst).  key32 and nonce12 are
  * host arrays.  Replaces chacha20_rfc8439_xor_cpu (csrc:2499-2523). */
 int32_t ztcp_chacha20_xor(const uint8_t* src, uint8_t* dst, int64_t len, const uint8_t key32[32], uint32_t counter,

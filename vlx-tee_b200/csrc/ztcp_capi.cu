@@ -160,46 +160,75 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
   return launch_status("mac_kernel<sign>");
 }
 
-int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_geometry* geom,
-                          const ztcp_page_batch* batch, const ztcp_keys* keys, uint16_t* out_k, uint16_t* out_v,
-                          int32_t* status, int32_t* any_fail, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// Shared argument checks and verify-pass parameters of ztcp_verify_pages / ztcp_decode_pages.
+int32_t prepare_verify(const uint8_t* blobs, int64_t blob_bytes, const ztcp_geometry* geom,
+                       const ztcp_page_batch* batch, const ztcp_keys* keys, int32_t* status, int32_t* any_fail,
+                       ztcp::MacParams* M) {
   int32_t rc = check_geometry(geom, "Invalid out_k_pages dimensions");
   if (rc != ZTCP_OK) return rc;
   if ((rc = check_batch(batch)) != ZTCP_OK) return rc;
   if (!keys) return fail(ZTCP_EINVAL, "keys must not be NULL");
-  if (!blobs || !out_k || !status || !any_fail)
-    return fail(ZTCP_EINVAL, "cold_blobs, out_k_pages, status and any_fail must not be NULL");
+  if (!blobs || !status || !any_fail) return fail(ZTCP_EINVAL, "cold_blobs, status and any_fail must not be NULL");
   if (blob_bytes <= ztcp::kHeaderBytes + ztcp::kTagBytes) return fail(ZTCP_EINVAL, "cold_blob too small");
+  memset(M, 0, sizeof(*M));
+  M->blobs = const_cast<uint8_t*>(blobs);
+  M->blob_stride = blob_bytes;
+  M->payload_len = blob_bytes - ztcp::kHeaderBytes - ztcp::kTagBytes;
+  M->n_pages = batch->n_pages;
+  M->mk0 = keys->mac[0];
+  M->mk1 = keys->mac[1];
+  M->meta = to_meta(batch);
+  M->vecs = geom->num_tokens * geom->num_heads;
+  M->head_dim = geom->head_dim;
+  M->rope_dim = geom->rope_dim;
+  M->has_v = geom->is_mla_single_buffer == 0;
+  M->status = status;
+  M->any_fail = any_fail;
+  return ZTCP_OK;
+}
+
+int32_t launch_verify(const ztcp::MacParams& M, cudaStream_t s) {
+  if (cudaMemsetAsync(M.any_fail, 0, sizeof(int32_t), s) != cudaSuccess) return launch_status("memset any_fail");
+  ztcp::launch_mac(M, true, s);
+  return launch_status("mac_kernel<verify>");
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t ztcp_verify_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_geometry* geom,
+                          const ztcp_page_batch* batch, const ztcp_keys* keys, int32_t* status, int32_t* any_fail,
+                          void* stream) {
+  ztcp::MacParams M;
+  const int32_t rc = prepare_verify(blobs, blob_bytes, geom, batch, keys, status, any_fail, &M);
+  if (rc != ZTCP_OK) return rc;
+  return launch_verify(M, static_cast<cudaStream_t>(stream));
+}
+
+int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_geometry* geom,
+                          const ztcp_page_batch* batch, const ztcp_keys* keys, uint16_t* out_k, uint16_t* out_v,
+                          int32_t* status, int32_t* any_fail, void* stream) {
+  ztcp::MacParams M;
+  int32_t rc = prepare_verify(blobs, blob_bytes, geom, batch, keys, status, any_fail, &M);
+  if (rc != ZTCP_OK) return rc;
+  if (!out_k) return fail(ZTCP_EINVAL, "out_k_pages must not be NULL");
   const bool has_v = geom->is_mla_single_buffer == 0;
   if (has_v && !out_v) return fail(ZTCP_EINVAL, "out_v_pages is required for non-MLA geometry");
   if (!has_v && out_v) return fail(ZTCP_EINVAL, "out_v_pages must be NULL for a single-buffer MLA geometry");
   if (!aligned16(out_k) || (out_v && !aligned16(out_v)))
     return fail(ZTCP_EINVAL, "out_k_pages / out_v_pages must be 16-byte aligned");
   const int64_t vecs = geom->num_tokens * geom->num_heads;
-  const int64_t payload_len = blob_bytes - ztcp::kHeaderBytes - ztcp::kTagBytes;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-
-  ztcp::MacParams M;
-  memset(&M, 0, sizeof(M));
-  M.blobs = const_cast<uint8_t*>(blobs);
-  M.blob_stride = blob_bytes;
-  M.payload_len = payload_len;
-  M.n_pages = batch->n_pages;
-  M.mk0 = keys->mac[0];
-  M.mk1 = keys->mac[1];
-  M.meta = to_meta(batch);
-  M.vecs = vecs;
-  M.head_dim = geom->head_dim;
-  M.rope_dim = geom->rope_dim;
-  M.has_v = has_v;
-  M.status = status;
-  M.any_fail = any_fail;
 
   ztcp::IngressParams P;
   memset(&P, 0, sizeof(P));
   P.blobs = blobs;
   P.blob_stride = blob_bytes;
-  P.payload_len = payload_len;
+  P.payload_len = M.payload_len;
   P.k_out = out_k;
   P.v_out = out_v;
   P.page_elems = vecs * geom->head_dim;
@@ -219,9 +248,8 @@ int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_g
   P.stage_bytes = (int32_t)(P.tile_vecs * worst + 6 * 16);
   if (P.n_pages * P.n_tiles > 0x7FFFFFFFLL) return fail(ZTCP_EINVAL, "batch too large for one launch");
 
-  if (cudaMemsetAsync(any_fail, 0, sizeof(int32_t), s) != cudaSuccess) return launch_status("memset any_fail");
-  ztcp::launch_mac(M, true, s);
-  if ((rc = launch_status("mac_kernel<verify>")) != ZTCP_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = launch_verify(M, s)) != ZTCP_OK) return rc;
   ztcp::launch_ingress(P, s);
   return launch_status("ingress_tile_kernel");
 }

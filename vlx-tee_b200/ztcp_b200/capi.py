@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "ztcp_spec_payload_bytes",
     "ztcp_encode_pages",
     "ztcp_decode_pages",
+    "ztcp_verify_pages",
     "ztcp_chacha20_xor",
     "ztcp_siphash24_128",
 )
@@ -105,6 +106,8 @@ def load() -> C.CDLL:
     L.ztcp_decode_pages.restype = i32
     L.ztcp_decode_pages.argtypes = [vp, i64, C.POINTER(Geometry), C.POINTER(PageBatch), C.POINTER(Keys), vp, vp,
                                     vp, vp, vp]
+    L.ztcp_verify_pages.restype = i32
+    L.ztcp_verify_pages.argtypes = [vp, i64, C.POINTER(Geometry), C.POINTER(PageBatch), C.POINTER(Keys), vp, vp, vp]
     L.ztcp_chacha20_xor.restype = i32
     L.ztcp_chacha20_xor.argtypes = [vp, vp, i64, C.c_char_p, u32, C.c_char_p, vp]
     L.ztcp_siphash24_128.restype = i32

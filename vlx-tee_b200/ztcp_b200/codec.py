@@ -161,6 +161,30 @@ def decode_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, out_k: torch.T
     return status, any_fail
 
 
+def verify_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, *, num_tokens: int, num_heads: int,
+                 head_dim: int, rope_dim: int, is_mla: bool, tenant_id_hash: int, model_id_hash: int, layer_id: int,
+                 keys: capi.Keys, layer_ids: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                 any_fail: torch.Tensor | None = None):
+    """Integrity check of stored blobs without decrypting; returns device (status[n], any_fail[1])."""
+    dev = blobs.device
+    _require_cuda("cold_blobs", blobs, (torch.uint8,))
+    if blobs.dim() != 2:
+        raise RuntimeError("cold_blobs must have shape [batch, total_blob_bytes]")
+    n, blob_bytes = blobs.shape
+    _check_meta(dev, n, None, None, layer_ids, token_hashes)
+    if status is None:
+        status = torch.empty(n, dtype=torch.int32, device=dev)
+    if any_fail is None:
+        any_fail = torch.empty(1, dtype=torch.int32, device=dev)
+    geom = capi.geometry(num_tokens, num_heads, head_dim, rope_dim, is_mla)
+    batch = _page_batch(n, token_hashes, None, None, layer_ids, 0, tenant_id_hash, model_id_hash, layer_id, 0)
+    with torch.cuda.device(dev):
+        rc = capi.load().ztcp_verify_pages(_ptr(blobs), int(blob_bytes), geom, batch, keys, _ptr(status),
+                                           _ptr(any_fail), _stream_handle(dev))
+    capi.check(rc)
+    return status, any_fail
+
+
 # Exception texts of the reference's batch and single-page decoders (csrc:2236-2244, :1582-1637).
 BATCH_MESSAGES = {
     capi.PAGE_BAD_MAGIC: "KV_INTEGRITY_ERROR: Invalid cold-page header magic, version, or flags",

@@ -35,7 +35,10 @@ def _device_of(*tensors) -> torch.device:
 def _to_dev(t: torch.Tensor | None, dev: torch.device) -> torch.Tensor | None:
     if t is None or (t.is_cuda and t.device == dev):
         return t
-    return t.pin_memory().to(dev, non_blocking=True) if not t.is_cuda else t.to(dev)
+    if t.is_cuda:
+        return t.to(dev)
+    src = t if t.is_pinned() else t.pin_memory()
+    return src.to(dev, non_blocking=True)
 
 
 def _hashes(t: torch.Tensor, n: int, dev: torch.device, name: str) -> torch.Tensor:
