@@ -21,7 +21,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -73,63 +72,65 @@ def committed_traffic():
 # clocks during the timed region
 # ------------------------------------------------------------------------------------------------
 class ClockSampler:
-    FIELDS = ("index,pci.bus_id,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Polls NVML every 5 ms from a background thread while the timed region runs (SM clock and clock
+    event reasons), so even a region of a few milliseconds gets samples."""
 
-    def __init__(self, bus_id: str | None):
-        self.bus_id = bus_id
-        self.proc = None
-        self.path = os.path.join("/tmp", f"ztcp_clocks_{os.getpid()}.csv")
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
+
+    def __init__(self, dev_index: int):
+        self.dev_index = dev_index
+        self.samples, self.reason_bits, self.max_mhz = [], 0, None
+        self._stop = None
+
+    def _handle(self, nv):
+        import torch
+
+        p = torch.cuda.get_device_properties(self.dev_index)
+        try:
+            return nv.nvmlDeviceGetHandleByPciBusId(f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0")
+        except Exception:  # noqa: BLE001  (older torch: no PCI ids; fall back to the visible-device order)
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[self.dev_index]) if vis else self.dev_index
+            return nv.nvmlDeviceGetHandleByIndex(idx)
 
     def __enter__(self):
+        import threading
+
         try:
-            self.f = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            import pynvml as nv
+
+            nv.nvmlInit()
+            h = self._handle(nv)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        except Exception:  # noqa: BLE001
+            return self
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append(float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)))
+                    self.reason_bits |= int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                except Exception:  # noqa: BLE001
+                    pass
+                self._stop.wait(0.005)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            self.f.close()
+        if self._stop is not None:
+            self._stop.set()
+            self._thread.join()
 
     def summary(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) < 10:
-                    continue
-                if self.bus_id and parts[1].upper() != self.bus_id.upper():
-                    continue
-                rows.append(parts)
-        os.unlink(self.path)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[6:10]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][3]),
-                "reasons": reasons, "samples": len(rows)}
-
-
-def bus_id_of(dev_index: int) -> str | None:
-    import torch
-
-    p = torch.cuda.get_device_properties(dev_index)
-    try:
-        return f"{p.pci_domain_id:08X}:{p.pci_bus_id:02X}:{p.pci_device_id:02X}.0"
-    except AttributeError:
-        return None
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["nvml unavailable"], "samples": 0}
+        reasons = sorted(n for b, n in self.REASONS.items() if self.reason_bits & b)
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(self.samples), "sm_mhz_min": min(self.samples)}
 
 
 # ------------------------------------------------------------------------------------------------
@@ -276,7 +277,7 @@ def ours(args):
 
     K = args.steps
     ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
-    with ClockSampler(bus_id_of(local)) as clocks:
+    with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
         for i in range(K):

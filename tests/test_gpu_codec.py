@@ -304,3 +304,46 @@ def test_fidelity_configs_2_and_3(ext):
     kd, _ = gpu_decode(ext, blobs, toks, tuple(kb.shape), 64, True, m)
     cos = helpers.attention_output_cosine(kb.float(), None, kd.cpu().float(), None, 16)
     assert cos > 0.99, cos
+
+
+def _tie_groups(qmax: int, n_groups: int, seed: int) -> np.ndarray:
+    """fp16 groups whose largest |x| fixes the scale and whose other elements make x * (1/scale) round
+    (in fp32) to an exact .5 tie while the unrounded product is not a tie: a fused multiply-add in place
+    of the multiply then the rounding add would break those ties differently."""
+    rng = np.random.default_rng(seed)
+    f32 = np.float32
+    out = []
+    while len(out) < n_groups:
+        amax = np.float16(rng.uniform(0.01, 300.0))
+        scale = np.float16(f32(amax) * (f32(1.0) / f32(qmax)))
+        if int(scale.view(np.uint16)) < 0x400:
+            continue
+        inv = f32(1.0) / f32(scale)
+        cand = rng.uniform(-float(amax), float(amax), 4096).astype(np.float16)
+        p32 = cand.astype(np.float32) * inv
+        exact = cand.astype(np.float64) * np.float64(inv)
+        frac = np.abs(p32 - np.trunc(p32))
+        ties = cand[(frac == 0.5) & (exact != p32.astype(np.float64))]
+        if len(ties) < 4:
+            continue
+        g = np.concatenate([[amax], ties[:15], np.zeros(15, np.float16)])[:16].astype(np.float16)
+        out.append(rng.permutation(g))
+    return np.stack(out)
+
+
+@pytest.mark.parametrize("preset,rope_mode", [(1, 0), (3, 0)])
+def test_rounding_ties_match_oracle(ext, oracle, preset, rope_mode):
+    from ztcp_b200 import workload
+
+    qmax = 7 if preset == 1 else 127
+    T, H, D = 8, 4, 64
+    groups = _tie_groups(qmax, 2 * T * H * D // 16, seed=preset)
+    k = groups[: T * H * D // 16].reshape(1, T, H, D)
+    v = groups[T * H * D // 16:].reshape(1, T, H, D)
+    m = workload.session_material(77)
+    toks = workload.token_hashes(1, 78)
+    exp = oracle.spec_payload_bytes(preset, rope_mode, T * H, D, 0, True)
+    blobs = gpu_encode(ext, torch.from_numpy(k), torch.from_numpy(v), torch.from_numpy(toks), 0, preset, rope_mode,
+                       exp, m)
+    want = helpers.oracle_encode(oracle, k, v, toks, 0, preset, rope_mode, exp, m)
+    np.testing.assert_array_equal(blobs.cpu().numpy(), want)

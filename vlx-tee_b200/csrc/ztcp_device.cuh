@@ -3,8 +3,9 @@
 //  * ChaCha20 (RFC 8439 section 2.3) keystream blocks, one 64-byte block per thread, counter-indexed
 //    so any block of a page's keystream is computed independently (reference: csrc:113-189).
 //  * SipHash-2-4 with 128-bit output as a serial per-lane chain over 64-bit words (csrc:401-471),
-//    written on 32-bit halves with explicit carry so each 64-bit add is one add.cc/addc pair and each
-//    rotate two funnel shifts (rotate by 32 is a register swap).
+//    written on 32-bit halves with explicit carry: each 64-bit add is one add.cc/addc pair, each
+//    rotate two funnel shifts or byte permutes (rotate by 32 is a register swap).  The chain is bound
+//    by the ALU pipe (~42 ALU instructions per word, 2 cycles each per warp on a sub-partition).
 //  * Group-16 INT8 / INT4 quantizers and dequantizers bit-exact with the reference's scalar x86 path
 //    (csrc:734-754, 771-777, 805-825, 845-854), including its handling of NaN products.
 #pragma once
@@ -88,10 +89,18 @@ struct SipState {
     v2 = w64(0x6c7967656e657261ull ^ k0);
     v3 = w64(0x7465646279746573ull ^ k1);
   }
-  __device__ __forceinline__ void round() {
+  // One SipRound.  The 64-bit rotate by 16 is two byte permutes; rotates by 13, 17 and 21 are funnel
+  // shifts; rotate by 32 swaps halves.  `pre` is XORed into v3 by the last instruction that writes it
+  // (a 3-input LOP3), which lets the next word's `v3 ^= m` ride along for free.
+  __device__ __forceinline__ void round(W64 pre = W64{0u, 0u}) {
     v0 = add64(v0, v1); v1 = xor64(rotl64<13>(v1), v0); v0 = rotl64<32>(v0);
-    v2 = add64(v2, v3); v3 = xor64(rotl64<16>(v3), v2);
-    v0 = add64(v0, v3); v3 = xor64(rotl64<21>(v3), v0);
+    v2 = add64(v2, v3);
+    v3 = W64{__byte_perm(v3.hi, v3.lo, 0x5432) ^ v2.lo, __byte_perm(v3.lo, v3.hi, 0x5432) ^ v2.hi};
+    v0 = add64(v0, v3);
+    {
+      const W64 r = rotl64<21>(v3);
+      v3 = W64{r.lo ^ v0.lo ^ pre.lo, r.hi ^ v0.hi ^ pre.hi};
+    }
     v2 = add64(v2, v1); v1 = xor64(rotl64<17>(v1), v2); v2 = rotl64<32>(v2);
   }
   __device__ __forceinline__ void absorb(W64 m) {
@@ -101,6 +110,12 @@ struct SipState {
     v0 = xor64(v0, m);
   }
   __device__ __forceinline__ void absorb(uint32_t lo, uint32_t hi) { absorb(W64{lo, hi}); }
+  // Absorb m into a state whose v3 already carries m, and fold the following word into v3.
+  __device__ __forceinline__ void absorb_pre(W64 m, W64 next) {
+    round();
+    round(next);
+    v0 = xor64(v0, m);
+  }
   // finalization: v2 ^= 0xee, 4 rounds -> low half; v1 ^= 0xdd, 4 rounds -> high half (csrc:458-470)
   __device__ __forceinline__ void finish(uint32_t tag[4]) {
     v2.lo ^= 0xeeu;
@@ -129,100 +144,234 @@ __device__ __forceinline__ int32_t x86_cvtt(float f) {
   return __float2int_rz(f);
 }
 
-// Loads 16 consecutive elements (fp16 or bf16 bits) as fp16 bit patterns.  src must be 16-byte aligned.
+// ------------------------------------------------------------------------------------------------
+// Group loads: 16 consecutive elements as eight fp16x2 words (bf16 input rounded to fp16 first)
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t w) {
+  const float2 f = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+  const __half2 h = __float22half2_rn(f);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// src must be 16-byte aligned.
 template <bool BF16>
-__device__ __forceinline__ void load_group16(const uint16_t* src, uint16_t h[16]) {
+__device__ __forceinline__ void load_group16(const uint16_t* src, uint32_t w[8]) {
   const uint4 a = __ldg(reinterpret_cast<const uint4*>(src));
   const uint4 b = __ldg(reinterpret_cast<const uint4*>(src) + 1);
-  const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+  if (BF16) {
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    h[2 * i] = (uint16_t)(w[i] & 0xFFFFu);
-    h[2 * i + 1] = (uint16_t)(w[i] >> 16);
-    if (BF16) {
-      h[2 * i] = bf16_bits_to_f16_bits(h[2 * i]);
-      h[2 * i + 1] = bf16_bits_to_f16_bits(h[2 * i + 1]);
-    }
+    for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
   }
 }
 
+__device__ __forceinline__ uint16_t lo16(uint32_t w) { return (uint16_t)(w & 0xFFFFu); }
+__device__ __forceinline__ uint16_t hi16(uint32_t w) { return (uint16_t)(w >> 16); }
+
+// Largest |x| bit pattern of the group.  For non-negative IEEE halves the bit patterns order like the
+// values, with +inf = 0x7C00 and NaN above it, so a result >= 0x7C00 flags a non-finite element.
+__device__ __forceinline__ uint32_t group_amax_bits(const uint32_t w[8]) {
+  uint32_t m = w[0] & 0x7FFF7FFFu;
+#pragma unroll
+  for (int i = 1; i < 8; ++i) m = __vmaxu2(m, w[i] & 0x7FFF7FFFu);
+  return max(m & 0xFFFFu, m >> 16);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Exact scalar quantizers (the reference's x86 semantics, including NaN products); used for groups
+// whose scale is subnormal, zero or non-finite, or that hold a non-finite element.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float f16_at(const uint32_t w[8], int i) {
+  return f16_bits_to_f32((i & 1) ? hi16(w[i >> 1]) : lo16(w[i >> 1]));
+}
+
 // amax with a 1e-6 floor; NaN elements never compare greater (csrc:737-744 / 808-815)
-__device__ __forceinline__ float group_amax(const uint16_t h[16]) {
+__device__ __forceinline__ float group_amax_exact(const uint32_t w[8]) {
   float amax = 1e-6f;
 #pragma unroll
   for (int i = 0; i < 16; ++i) {
-    const float av = fabsf(f16_bits_to_f32(h[i]));
+    const float av = fabsf(f16_at(w, i));
     amax = av > amax ? av : amax;
   }
   return amax;
 }
 
-// INT8: scale = fp16(amax / 127), q = clamp(rint(x * (1 / scale)), -127, 127); a NaN product
-// quantizes to +127 (reference x86 build, pinned by the oracle).
-__device__ __forceinline__ uint16_t quant_int8(const uint16_t h[16], uint32_t q[4]) {
-  const float amax = group_amax(h);
-  const __half sh = __float2half_rn(__fdiv_rn(amax, 127.0f));
-  const float inv = __frcp_rn(__half2float(sh));
+// INT8: q = clamp(rint(x * inv), -127, 127); a NaN product quantizes to +127.
+__device__ __forceinline__ void quant_int8_exact(const uint32_t w[8], float inv, uint32_t q[4]) {
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
+  for (int k = 0; k < 4; ++k) {
     uint32_t word = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      float qf = rintf(__fmul_rn(f16_bits_to_f32(h[4 * w + j]), inv));
+      float qf = rintf(__fmul_rn(f16_at(w, 4 * k + j), inv));
       if (qf != qf) qf = 127.0f;
       qf = fminf(fmaxf(qf, -127.0f), 127.0f);
       word |= ((uint32_t)(__float2int_rz(qf)) & 0xFFu) << (8 * j);
     }
-    q[w] = word;
+    q[k] = word;
   }
-  return __half_as_ushort(sh);
 }
 
-// INT4: scale = fp16(amax / 7), u = clamp(int(rint(x * (1 / scale)) + 8), 0, 15) with x86 float->int
-// conversion; byte i = u[2i] | u[2i+1] << 4.
-__device__ __forceinline__ uint16_t quant_int4(const uint16_t h[16], uint32_t q[2]) {
-  const float amax = group_amax(h);
-  const __half sh = __float2half_rn(__fdiv_rn(amax, 7.0f));
-  const float inv = __frcp_rn(__half2float(sh));
+// INT4: u = clamp(int(rint(x * inv) + 8), 0, 15) with x86 float->int conversion (NaN -> 0).
+__device__ __forceinline__ void quant_int4_exact(const uint32_t w[8], float inv, uint32_t q[2]) {
 #pragma unroll
-  for (int w = 0; w < 2; ++w) {
+  for (int k = 0; k < 2; ++k) {
     uint32_t word = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float qf = __fadd_rn(rintf(__fmul_rn(f16_bits_to_f32(h[8 * w + j]), inv)), 8.0f);
-      const int32_t u = min(max(x86_cvtt(qf), 0), 15);
-      word |= (uint32_t)u << (4 * j);
+      const float qf = __fadd_rn(rintf(__fmul_rn(f16_at(w, 8 * k + j), inv)), 8.0f);
+      word |= (uint32_t)min(max(x86_cvtt(qf), 0), 15) << (4 * j);
     }
-    q[w] = word;
+    q[k] = word;
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Group-16 quantizers.  scale = fp16(amax / qmax) and inv = 1 / float(scale) (IEEE reciprocal).
+// Fast path: every element finite and scale a normal fp16.  Then the scale is within 2^-11 of
+// amax / qmax, so |x * inv| <= qmax * (1 + 2^-11) + tiny < qmax + 0.5 and no clamp can fire; rint is
+// the FADD of 1.5 * 2^23 (round-to-nearest-even at integer granularity, exact for |p| < 2^22) whose
+// low bits are rint(p) in two's complement.  fp16(amax / qmax) equals fp16(amax * (1 / qmax)) for
+// every fp16 amax and the 1e-6 floor (checked exhaustively by the CPU tests), so the scale is one
+// multiply.
+// ------------------------------------------------------------------------------------------------
+constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+
+// x * inv rounded to fp32, then + 1.5 * 2^23 rounded again.  Both steps are the scalar _rn intrinsics,
+// which are never contracted into a fused multiply-add: a fused x * inv + 1.5 * 2^23 would break
+// rounding ties (p = k + 0.5 after the fp32 multiply) with the unrounded product.  (Packed f32x2
+// multiply and add were observed to be fused on sm_100a even with explicit .rn, so they are not used.)
+__device__ __forceinline__ uint32_t round_bits(float x, float inv) {
+  return __float_as_uint(__fadd_rn(__fmul_rn(x, inv), kRoundMagic));
+}
+
+__device__ __forceinline__ bool group_scale(const uint32_t w[8], float rq, __half* sh, float* inv) {
+  const uint32_t amax_bits = group_amax_bits(w);
+  if (amax_bits >= 0x7C00u) {  // inf or NaN element: exact path computes everything
+    *sh = __float2half_rn(__fmul_rn(group_amax_exact(w), rq));
+    *inv = __frcp_rn(__half2float(*sh));
+    return false;
+  }
+  const float amax = fmaxf(f16_bits_to_f32((uint16_t)amax_bits), 1e-6f);
+  *sh = __float2half_rn(__fmul_rn(amax, rq));
+  *inv = __frcp_rn(__half2float(*sh));
+  return __half_as_ushort(*sh) >= 0x0400u;  // normal scale (finite: amax <= 65504)
+}
+
+__device__ __forceinline__ uint16_t quant_int8(const uint32_t w[8], uint32_t q[4]) {
+  __half sh;
+  float inv;
+  if (!group_scale(w, 1.0f / 127.0f, &sh, &inv)) {
+    quant_int8_exact(w, inv, q);
+    return __half_as_ushort(sh);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * k]));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * k + 1]));
+    const uint32_t ab = __byte_perm(round_bits(a.x, inv), round_bits(a.y, inv), 0x0040);
+    const uint32_t cd = __byte_perm(round_bits(b.x, inv), round_bits(b.y, inv), 0x0040);
+    q[k] = __byte_perm(ab, cd, 0x5410);
   }
   return __half_as_ushort(sh);
 }
 
-// fp16(float(q) * float(scale)); a NaN product (zero times an infinite scale) is written as 0xFE00,
-// the half the reference's x86 build produces from the default NaN.
+__device__ __forceinline__ uint16_t quant_int4(const uint32_t w[8], uint32_t q[2]) {
+  __half sh;
+  float inv;
+  if (!group_scale(w, 1.0f / 7.0f, &sh, &inv)) {
+    quant_int4_exact(w, inv, q);
+    return __half_as_ushort(sh);
+  }
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    uint32_t acc = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[4 * k + j]));
+      // nibble = rint(p) mod 16; +8 is applied to all eight nibbles at once below (flip bit 3)
+      acc |= (round_bits(x.x, inv) & 0xFu) << (8 * j);
+      acc |= (round_bits(x.y, inv) & 0xFu) << (8 * j + 4);
+    }
+    q[k] = acc ^ 0x88888888u;
+  }
+  return __half_as_ushort(sh);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Dequantizers: fp16(float(q) * float(scale)).  float(q) * float(scale) is exact in fp32 (<= 8 + 11
+// significant bits), so one IEEE half multiply of half(q) by the scale rounds it identically; half(q)
+// is built exactly as (1024 + u) - bias from the bit pattern 0x6400 | u.  A non-finite scale takes the
+// exact path, which writes a NaN product as 0xFE00 -- the half the reference's x86 build produces from
+// the default NaN.
+// ------------------------------------------------------------------------------------------------
 __device__ __forceinline__ uint16_t dequant_one(float q, float s) {
   const float p = __fmul_rn(q, s);
   if (p != p) return 0xFE00u;
   return __half_as_ushort(__float2half_rn(p));
 }
 
-__device__ __forceinline__ void dequant_int8(const uint32_t q[4], uint16_t scale, uint32_t out[8]) {
+__device__ __forceinline__ void dequant_exact(const uint32_t* q, int bits, uint16_t scale, uint32_t out[8]) {
   const float s = f16_bits_to_f32(scale);
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const uint32_t w = q[i / 2] >> (16 * (i & 1));
-    const float a = (float)(int8_t)(w & 0xFFu), b = (float)(int8_t)((w >> 8) & 0xFFu);
+    float a, b;
+    if (bits == 8) {
+      const uint32_t w = q[i / 2] >> (16 * (i & 1));
+      a = (float)(int8_t)(w & 0xFFu);
+      b = (float)(int8_t)((w >> 8) & 0xFFu);
+    } else {
+      const uint32_t byte = (q[i / 4] >> (8 * (i & 3))) & 0xFFu;
+      a = (float)(int)(byte & 0xFu) - 8.0f;
+      b = (float)(int)(byte >> 4) - 8.0f;
+    }
     out[i] = (uint32_t)dequant_one(a, s) | ((uint32_t)dequant_one(b, s) << 16);
   }
 }
 
-__device__ __forceinline__ void dequant_int4(const uint32_t q[2], uint16_t scale, uint32_t out[8]) {
-  const float s = f16_bits_to_f32(scale);
+__device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
+__device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<const __half2*>(&u); }
+
+__device__ __forceinline__ void dequant_int8(const uint32_t q[4], uint16_t scale, uint32_t out[8]) {
+  if ((scale & 0x7C00u) == 0x7C00u) {
+    dequant_exact(q, 8, scale, out);
+    return;
+  }
+  const __half2 s2 = __half2half2(__ushort_as_half(scale));
+  const __half2 bias = __float2half2_rn(1152.0f);  // 0x6400 | (q ^ 0x80) = 1152 + q
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const uint32_t byte = (q[i / 4] >> (8 * (i & 3))) & 0xFFu;
-    const float a = (float)(int)(byte & 0xFu) - 8.0f, b = (float)(int)(byte >> 4) - 8.0f;
-    out[i] = (uint32_t)dequant_one(a, s) | ((uint32_t)dequant_one(b, s) << 16);
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t u = q[k] ^ 0x80808080u;
+    const uint32_t lo = __byte_perm(u, 0x64646464u, 0x5140), hi = __byte_perm(u, 0x64646464u, 0x7362);
+    out[2 * k] = h2_bits(__hmul2_rn(__hsub2(bits_h2(lo), bias), s2));
+    out[2 * k + 1] = h2_bits(__hmul2_rn(__hsub2(bits_h2(hi), bias), s2));
+  }
+}
+
+__device__ __forceinline__ void dequant_int4(const uint32_t q[2], uint16_t scale, uint32_t out[8]) {
+  if ((scale & 0x7C00u) == 0x7C00u) {
+    dequant_exact(q, 4, scale, out);
+    return;
+  }
+  const __half2 s2 = __half2half2(__ushort_as_half(scale));
+  const __half2 bias = __float2half2_rn(1032.0f);  // 0x6400 | u = 1024 + u, q = u - 8
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    const uint32_t w = q[k];  // nibbles e0..e7 of this word, element i at bits 4i
+    // (e0,e4) (e1,e5) (e2,e6) (e3,e7) as fp16 pairs 1024 + u
+    const uint32_t p0 = (w & 0x000F000Fu) | 0x64006400u;
+    const uint32_t p1 = ((w >> 4) & 0x000F000Fu) | 0x64006400u;
+    const uint32_t p2 = ((w >> 8) & 0x000F000Fu) | 0x64006400u;
+    const uint32_t p3 = ((w >> 12) & 0x000F000Fu) | 0x64006400u;
+    const __half2 v0 = __hmul2_rn(__hsub2(bits_h2(p0), bias), s2);
+    const __half2 v1 = __hmul2_rn(__hsub2(bits_h2(p1), bias), s2);
+    const __half2 v2 = __hmul2_rn(__hsub2(bits_h2(p2), bias), s2);
+    const __half2 v3 = __hmul2_rn(__hsub2(bits_h2(p3), bias), s2);
+    out[4 * k + 0] = __byte_perm(h2_bits(v0), h2_bits(v1), 0x5410);  // (e0, e1)
+    out[4 * k + 1] = __byte_perm(h2_bits(v2), h2_bits(v3), 0x5410);  // (e2, e3)
+    out[4 * k + 2] = __byte_perm(h2_bits(v0), h2_bits(v1), 0x7632);  // (e4, e5)
+    out[4 * k + 3] = __byte_perm(h2_bits(v2), h2_bits(v3), 0x7632);  // (e6, e7)
   }
 }
 

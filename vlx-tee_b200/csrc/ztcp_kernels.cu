@@ -62,7 +62,31 @@ __device__ __forceinline__ int64_t range_blocks(const Range& r) {
   return r.b > r.a ? ((r.b - 1) >> 6) - (r.a >> 6) + 1 : 0;
 }
 
-__device__ __forceinline__ uint32_t pack2(uint16_t a, uint16_t b) { return (uint32_t)a | ((uint32_t)b << 16); }
+// A tile's byte ranges and the prefix sums of their 64-byte keystream blocks, built once per CTA in
+// shared memory; threads then map a flat keystream-block index to (range, block) by a short scan.
+struct RangeTable {
+  Range r[7];
+  int64_t first[8];  // first[i] = flat index of range i's first block; first[n] = total blocks
+  int32_t n;
+};
+
+__device__ __forceinline__ void build_range_table(RangeTable& T, const Layout& L, int64_t v0, int tv,
+                                                  const int32_t sq[3], const int32_t ss[3], bool with_pad,
+                                                  int64_t payload_len) {
+  T.n = tile_ranges(L, v0, tv, sq, ss, with_pad, payload_len, T.r);
+  int64_t acc = 0;
+  for (int i = 0; i < T.n; ++i) {
+    T.first[i] = acc;
+    acc += range_blocks(T.r[i]);
+  }
+  T.first[T.n] = acc;
+}
+
+__device__ __forceinline__ int find_range(const RangeTable& T, int64_t bi) {
+  int i = 0;
+  while (i + 1 < T.n && bi >= T.first[i + 1]) ++i;
+  return i;
+}
 
 // XOR one keystream block into bytes [lo, hi) of dst, taking plaintext from src (nullptr = zeros).
 // Both pointers address payload byte 64*kb (block start); bytes outside [lo, hi) are untouched.
@@ -84,10 +108,13 @@ __device__ __forceinline__ void xor_block_bytes(uint8_t* dst, const uint8_t* src
 template <bool BF16>
 __global__ void __launch_bounds__(kTileThreads) egress_tile_kernel(const __grid_constant__ EgressParams P) {
   extern __shared__ __align__(16) uint8_t stage[];
+  __shared__ RangeTable T;
   const int64_t page = blockIdx.x / P.n_tiles;
   const int tile = (int)(blockIdx.x - page * P.n_tiles);
   const int64_t v0 = (int64_t)tile * P.tile_vecs;
   const int tv = (int)min((int64_t)P.tile_vecs, P.vecs - v0);
+  if (threadIdx.x == 0)
+    build_range_table(T, P.L, v0, tv, P.stage_q, P.stage_s, tile == P.n_tiles - 1, P.payload_len);
   const int64_t blk = page_block(P.meta, page);
   const uint16_t* kp = P.k + blk * P.page_elems;
   const uint16_t* vp = P.v ? P.v + blk * P.page_elems : nullptr;
@@ -108,22 +135,22 @@ __global__ void __launch_bounds__(kTileThreads) egress_tile_kernel(const __grid_
     const int groups = S.dim >> 4;
     const int vec = local / groups, g = local - vec * groups;
     const uint16_t* src = (S.buf ? vp : kp) + (v0 + vec) * P.head_dim + S.col + g * 16;
-    uint16_t h[16];
-    load_group16<BF16>(src, h);
+    uint32_t w[8];
+    load_group16<BF16>(src, w);
     uint8_t* qd = stage + (s == 0 ? P.stage_q[0] : (s == 1 ? P.stage_q[1] : P.stage_q[2])) + vec * S.q_bpv;
     uint8_t* sd = stage + (s == 0 ? P.stage_s[0] : (s == 1 ? P.stage_s[1] : P.stage_s[2])) + vec * S.s_bpv;
     if (S.kind == kRaw) {
       uint4* d = reinterpret_cast<uint4*>(qd + g * 32);
-      d[0] = make_uint4(pack2(h[0], h[1]), pack2(h[2], h[3]), pack2(h[4], h[5]), pack2(h[6], h[7]));
-      d[1] = make_uint4(pack2(h[8], h[9]), pack2(h[10], h[11]), pack2(h[12], h[13]), pack2(h[14], h[15]));
+      d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      d[1] = make_uint4(w[4], w[5], w[6], w[7]);
     } else if (S.kind == kInt8) {
       uint32_t q[4];
-      const uint16_t sc = quant_int8(h, q);
+      const uint16_t sc = quant_int8(w, q);
       *reinterpret_cast<uint4*>(qd + g * 16) = make_uint4(q[0], q[1], q[2], q[3]);
       *reinterpret_cast<uint16_t*>(sd + g * 2) = sc;
     } else {
       uint32_t q[2];
-      const uint16_t sc = quant_int4(h, q);
+      const uint16_t sc = quant_int4(w, q);
       *reinterpret_cast<uint2*>(qd + g * 8) = make_uint2(q[0], q[1]);
       *reinterpret_cast<uint16_t*>(sd + g * 2) = sc;
     }
@@ -154,23 +181,13 @@ __global__ void __launch_bounds__(kTileThreads) egress_tile_kernel(const __grid_
   __syncthreads();
 
   // ---- phase 2: encrypt this tile's byte ranges
-  Range R[7];
-  const int nr = tile_ranges(P.L, v0, tv, P.stage_q, P.stage_s, tile == P.n_tiles - 1, P.payload_len, R);
-  int64_t nb[7];
-  int64_t total_blocks = 0;
-#pragma unroll
-  for (int i = 0; i < 7; ++i) {
-    nb[i] = i < nr ? range_blocks(R[i]) : 0;
-    total_blocks += nb[i];
-  }
+  const int64_t total_blocks = T.first[T.n];
   const uint32_t n2 = ((uint32_t)layer << 16) | P.meta.head_group;
   uint8_t* payload = blob + kHeaderBytes;
   for (int64_t bi = threadIdx.x; bi < total_blocks; bi += blockDim.x) {
-    int i = 0;
-    int64_t local = bi;
-    while (i < nr - 1 && local >= nb[i]) { local -= nb[i]; ++i; }
-    const Range r = R[i];
-    const int64_t kb = (r.a >> 6) + local;
+    const int i = find_range(T, bi);
+    const Range r = T.r[i];
+    const int64_t kb = (r.a >> 6) + (bi - T.first[i]);
     uint32_t ks[16];
     chacha20_block(P.key, (uint32_t)(1 + kb), (uint32_t)seq, (uint32_t)(seq >> 32), n2, ks);
     const int64_t base = kb << 6;
@@ -198,61 +215,111 @@ __device__ __forceinline__ uint32_t ld_u32_any(const uint8_t* p) {
   return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
 }
 
-// Absorbs bytes [0, len) of p as little-endian words plus the length word (csrc:425-442) and
-// finalizes.  The 16-byte-aligned path keeps one 128-byte chunk in flight ahead of the chain.
-__device__ __forceinline__ void siphash_bytes(SipState& st, const uint8_t* p, int64_t len, uint32_t tag[4]) {
+__device__ __forceinline__ W64 load_word_any(const uint8_t* p) { return W64{ld_u32_any(p), ld_u32_any(p + 4)}; }
+
+// Shared-memory ring of one chain lane: kRing chunks of 128 bytes (16 words), filled ahead of the chain
+// by per-thread asynchronous copies (cp.async, 16 bytes each, completed by cp.async.wait_group -- a
+// wait on the thread's own copies, which always finish).  The chain consumes ~8 bytes per ~86 cycles,
+// so 7 chunks in flight are ~9.6k cycles of lookahead: DRAM latency is hidden whether or not the blob
+// is L2-resident.  Lanes' rings are kRingStride apart (1040 = 65 x 16 bytes) so that the 16-byte reads
+// of 8 consecutive lanes fall in distinct bank quads.
+constexpr int kChunk = 128;
+constexpr int kRing = 8;
+constexpr int kRingStride = kRing * kChunk + 16;
+constexpr int kChainThreads = 128;
+constexpr int kRingBytes = kChainThreads * kRingStride;  // 133,120 bytes per chain CTA
+
+__device__ __forceinline__ void cp_async16(uint32_t smem_addr, const void* gptr) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr), "l"(gptr) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+__device__ __forceinline__ void ring_fill(uint32_t ring, const uint8_t* p, int64_t chunk, int64_t n_chunks) {
+  if (chunk < n_chunks) {
+    const uint32_t dst = ring + (uint32_t)(chunk & (kRing - 1)) * kChunk;
+    const uint8_t* src = p + chunk * kChunk;
+#pragma unroll
+    for (int j = 0; j < kChunk / 16; ++j) cp_async16(dst + 16 * j, src + 16 * j);
+  }
+  cp_async_commit();  // empty groups past the end keep the group count uniform
+}
+
+// SipHash-2-4-128 of bytes [0, len) of p: little-endian words, then the length word (csrc:425-442),
+// then finalization.  Each word's `v3 ^= m` is folded into the previous word (absorb_pre), so the
+// stream is walked with one word of lookahead.  With a 16-byte-aligned p (and a ring, i.e. in the
+// chain kernel), whole 128-byte chunks stream through the lane's shared-memory ring; the remainder
+// and unaligned blobs use direct loads.
+__device__ __forceinline__ void siphash_bytes(SipState& st, const uint8_t* p, int64_t len, uint32_t tag[4],
+                                              uint8_t* ring_ptr) {
   const int64_t n_words = len >> 3;
-  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
-    const uint4* src = reinterpret_cast<const uint4*>(p);
-    const int64_t n_vec = n_words >> 1;
-    const int64_t n_chunks = n_vec >> 3;
-    uint4 cur[8];
-    if (n_chunks > 0) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) cur[j] = __ldg(src + j);
+  W64 fin{0u, (uint32_t)(len & 0xff) << 24};
+  {
+    const int rem = (int)(len & 7);
+    const uint8_t* t = p + n_words * 8;
+    for (int b = 0; b < rem; ++b) {
+      if (b < 4) fin.lo |= (uint32_t)t[b] << (8 * b);
+      else fin.hi |= (uint32_t)t[b] << (8 * (b - 4));
     }
-    for (int64_t c = 0; c < n_chunks; ++c) {
-      uint4 nxt[8];
-      const bool more = c + 1 < n_chunks;
-      if (more) {
+  }
+  int64_t i0 = 0;  // first word not yet absorbed
+  if (ring_ptr != nullptr && (reinterpret_cast<uintptr_t>(p) & 15) == 0 && n_words >= 32) {
+    const int64_t n_chunks = n_words >> 4;
+    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(ring_ptr);
+    auto slot = [&](int64_t c) { return reinterpret_cast<const uint4*>(ring_ptr + (c & (kRing - 1)) * kChunk); };
+#pragma unroll 1
+    for (int c = 0; c < kRing - 1; ++c) ring_fill(ring, p, c, n_chunks);
+    const W64 after = n_chunks * 16 < n_words ? load_word_any(p + n_chunks * kChunk) : fin;
+    cp_async_wait<kRing - 2>();  // chunk 0 landed
+    uint4 A[8], B[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) nxt[j] = __ldg(src + (c + 1) * 8 + j);
-      }
+    for (int j = 0; j < 8; ++j) A[j] = slot(0)[j];
+    st.v3 = xor64(st.v3, W64{A[0].x, A[0].y});
+    // Chunk c is in registers when iteration c starts; the iteration refills the ring, waits for chunk
+    // c+1, reads it into the other register buffer (its latency hidden by absorbing chunk c) and
+    // absorbs chunk c, whose last word looks ahead into chunk c+1.
+    auto absorb_chunk = [&](const uint4 (&X)[8], W64 nx) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        st.absorb(cur[j].x, cur[j].y);
-        st.absorb(cur[j].z, cur[j].w);
+        st.absorb_pre(W64{X[j].x, X[j].y}, W64{X[j].z, X[j].w});
+        st.absorb_pre(W64{X[j].z, X[j].w}, j < 7 ? W64{X[j + 1].x, X[j + 1].y} : nx);
       }
-      if (more) {
+    };
+#pragma unroll 1
+    for (int64_t c = 0; c < n_chunks; c += 2) {
+      ring_fill(ring, p, c + kRing - 1, n_chunks);
+      cp_async_wait<kRing - 2>();  // chunk c+1 landed
+      const bool has1 = c + 1 < n_chunks;
+      if (has1) {
 #pragma unroll
-        for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+        for (int j = 0; j < 8; ++j) B[j] = slot(c + 1)[j];
       }
+      absorb_chunk(A, has1 ? W64{B[0].x, B[0].y} : after);
+      if (!has1) break;
+      ring_fill(ring, p, c + kRing, n_chunks);
+      cp_async_wait<kRing - 2>();  // chunk c+2 landed
+      const bool has2 = c + 2 < n_chunks;
+      if (has2) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) A[j] = slot(c + 2)[j];
+      }
+      absorb_chunk(B, has2 ? W64{A[0].x, A[0].y} : after);
     }
-    for (int64_t i = n_chunks * 8; i < n_vec; ++i) {
-      const uint4 t = __ldg(src + i);
-      st.absorb(t.x, t.y);
-      st.absorb(t.z, t.w);
-    }
-    if (n_words & 1) {
-      const uint2 t = __ldg(reinterpret_cast<const uint2*>(p + (n_words - 1) * 8));
-      st.absorb(t.x, t.y);
-    }
+    cp_async_wait<0>();
+    i0 = n_chunks * 16;
   } else {
-    for (int64_t i = 0; i < n_words; ++i) st.absorb(ld_u32_any(p + 8 * i), ld_u32_any(p + 8 * i + 4));
+    st.v3 = xor64(st.v3, n_words > 0 ? load_word_any(p) : fin);
   }
-  uint32_t lo = 0, hi = (uint32_t)(len & 0xff) << 24;
-  const int rem = (int)(len & 7);
-  const uint8_t* t = p + n_words * 8;
-  for (int b = 0; b < rem; ++b) {
-    if (b < 4) lo |= (uint32_t)t[b] << (8 * b);
-    else hi |= (uint32_t)t[b] << (8 * (b - 4));
-  }
-  st.absorb(lo, hi);
+  for (int64_t i = i0; i < n_words; ++i)
+    st.absorb_pre(load_word_any(p + 8 * i), i + 1 < n_words ? load_word_any(p + 8 * (i + 1)) : fin);
+  st.absorb_pre(fin, W64{0u, 0u});
   st.finish(tag);
 }
 
 template <bool VERIFY>
-__global__ void __launch_bounds__(128) mac_kernel(const __grid_constant__ MacParams P) {
+__global__ void __launch_bounds__(kChainThreads, 1) mac_kernel(const __grid_constant__ MacParams P) {
+  extern __shared__ __align__(16) uint8_t rings[];
   const int64_t page = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (page >= P.n_pages) return;
   uint8_t* blob = P.blobs + page * P.blob_stride;
@@ -276,7 +343,7 @@ __global__ void __launch_bounds__(128) mac_kernel(const __grid_constant__ MacPar
   SipState st;
   st.init(P.mk0, P.mk1);
   uint32_t tag[4];
-  siphash_bytes(st, blob, mac_len, tag);
+  siphash_bytes(st, blob, mac_len, tag, rings + threadIdx.x * kRingStride);
   uint8_t* tag_ptr = blob + mac_len;
   if (!VERIFY) {
     if ((reinterpret_cast<uintptr_t>(tag_ptr) & 3) == 0) {
@@ -330,34 +397,33 @@ __global__ void __launch_bounds__(kTileThreads) ingress_tile_kernel(const __grid
   }
 
   const uint8_t* blob = P.blobs + page * P.blob_stride;
-  const uint8_t flags = blob[3];
-  const uint32_t layer_hg = ld_u32_any(blob + 12);
-  const uint64_t seq = ((uint64_t)ld_u32_any(blob + 28) << 32) | ld_u32_any(blob + 24);
-  Layout L;
-  build_layout(flags & 0x0F, (flags >> 4) & 0x0F, P.vecs, P.head_dim, P.rope_dim, P.has_v != 0, &L);
-  int32_t sq[3], ss[3];
-  plan_stage(L, P.tile_vecs, sq, ss);
+  __shared__ RangeTable T;
+  __shared__ Layout sL;
+  __shared__ int32_t s_sq[3], s_ss[3];
+  __shared__ uint32_t s_n0, s_n1, s_n2;
+  if (threadIdx.x == 0) {
+    const uint8_t flags = blob[3];
+    const uint32_t layer_hg = ld_u32_any(blob + 12);
+    s_n0 = ld_u32_any(blob + 24);                  // sequence_nonce low word
+    s_n1 = ld_u32_any(blob + 28);                  // sequence_nonce high word
+    s_n2 = (layer_hg << 16) | (layer_hg >> 16);    // layer_id << 16 | head_group_id
+    build_layout(flags & 0x0F, (flags >> 4) & 0x0F, P.vecs, P.head_dim, P.rope_dim, P.has_v != 0, &sL);
+    plan_stage(sL, P.tile_vecs, s_sq, s_ss);
+    build_range_table(T, sL, v0, tv, s_sq, s_ss, false, P.payload_len);
+  }
+  __syncthreads();
+  const Layout& L = sL;
 
   // ---- phase 1: decrypt this tile's byte ranges into shared memory
-  Range R[7];
-  const int nr = tile_ranges(L, v0, tv, sq, ss, false, P.payload_len, R);
-  int64_t nb[7];
-  int64_t total_blocks = 0;
-#pragma unroll
-  for (int i = 0; i < 7; ++i) {
-    nb[i] = i < nr ? range_blocks(R[i]) : 0;
-    total_blocks += nb[i];
-  }
-  const uint32_t n2 = (layer_hg << 16) | (layer_hg >> 16);  // layer_id << 16 | head_group_id
+  const int64_t total_blocks = T.first[T.n];
+  const uint32_t n0 = s_n0, n1 = s_n1, n2 = s_n2;
   const uint8_t* payload = blob + kHeaderBytes;
   for (int64_t bi = threadIdx.x; bi < total_blocks; bi += blockDim.x) {
-    int i = 0;
-    int64_t local = bi;
-    while (i < nr - 1 && local >= nb[i]) { local -= nb[i]; ++i; }
-    const Range r = R[i];
-    const int64_t kb = (r.a >> 6) + local;
+    const int i = find_range(T, bi);
+    const Range r = T.r[i];
+    const int64_t kb = (r.a >> 6) + (bi - T.first[i]);
     uint32_t ks[16];
-    chacha20_block(P.key, (uint32_t)(1 + kb), (uint32_t)seq, (uint32_t)(seq >> 32), n2, ks);
+    chacha20_block(P.key, (uint32_t)(1 + kb), n0, n1, n2, ks);
     const int64_t base = kb << 6;
     const int lo = (int)(max(r.a, base) - base), hi = (int)(min(r.b, base + 64) - base);
     const uint8_t* src = payload + base;
@@ -399,8 +465,8 @@ __global__ void __launch_bounds__(kTileThreads) ingress_tile_kernel(const __grid
     const int groups = S.dim >> 4;
     const int vec = local / groups, g = local - vec * groups;
     uint4* dst = reinterpret_cast<uint4*>((S.buf ? vd : kd) + (v0 + vec) * P.head_dim + S.col + g * 16);
-    const uint8_t* qs = stage + (s == 0 ? sq[0] : (s == 1 ? sq[1] : sq[2])) + vec * S.q_bpv;
-    const uint8_t* sc = stage + (s == 0 ? ss[0] : (s == 1 ? ss[1] : ss[2])) + vec * S.s_bpv + g * 2;
+    const uint8_t* qs = stage + s_sq[s] + vec * S.q_bpv;
+    const uint8_t* sc = stage + s_ss[s] + vec * S.s_bpv + g * 2;
     uint32_t o[8];
     if (S.kind == kRaw) {
       const uint4* q = reinterpret_cast<const uint4*>(qs + g * 32);
@@ -450,10 +516,13 @@ __global__ void siphash_kernel(const uint8_t* src, int64_t len, uint64_t k0, uin
   SipState st;
   st.init(k0, k1);
   uint32_t tag[4];
-  siphash_bytes(st, src, len, tag);
+  siphash_bytes(st, src, len, tag, nullptr);
 #pragma unroll
   for (int i = 0; i < 16; ++i) out16[i] = (uint8_t)(tag[i >> 2] >> (8 * (i & 3)));
 }
+
+// Shared memory a chain CTA takes: the sm_100 per-CTA maximum (227 KB), so it owns its SM.
+constexpr int kMacReserveBytes = 227 * 1024;
 
 template <typename K>
 void ensure_smem(K kernel, int32_t bytes) {
@@ -474,9 +543,19 @@ void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream) {
 }
 
 void launch_mac(const MacParams& P, bool verify, cudaStream_t stream) {
-  const unsigned grid = (unsigned)((P.n_pages + 127) / 128);
-  if (verify) mac_kernel<true><<<grid, 128, 0, stream>>>(P);
-  else mac_kernel<false><<<grid, 128, 0, stream>>>(P);
+  // A chain CTA is four warps, one per SM sub-partition, each running 32 independent per-page chains
+  // that keep the sub-partition's ALU pipe busy.  The CTA takes the SM's whole shared memory (its
+  // lanes' input rings use 194 KB of it) so that no other CTA -- another chain CTA or a tile kernel
+  // running concurrently on another stream -- is co-scheduled on its sub-partitions.
+  static_assert(kRingBytes <= kMacReserveBytes, "chain rings must fit the reserved shared memory");
+  const unsigned grid = (unsigned)((P.n_pages + kChainThreads - 1) / kChainThreads);
+  if (verify) {
+    cudaFuncSetAttribute(mac_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMacReserveBytes);
+    mac_kernel<true><<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
+  } else {
+    cudaFuncSetAttribute(mac_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMacReserveBytes);
+    mac_kernel<false><<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
+  }
 }
 
 void launch_ingress(const IngressParams& P, cudaStream_t stream) {
