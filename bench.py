@@ -26,6 +26,10 @@ import time
 
 REPO = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(REPO, "vlx-tee_b200"))
+# One hardware work queue per in-flight batch (the driver default is 8; a batch waiting on its own
+# 0.6 ms tag chain would otherwise stall the batches that share its queue).  Process-local: read by
+# the CUDA driver when this process creates its context.
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
 
 PAGE_HOT_BYTES = 2 * 64 * 8 * 128 * 2       # K + V, bf16/fp16
 EXPECTED_PAYLOAD = 98304                     # INT4_SYM + PRESERVE_FP8, GQA 64x8x128
@@ -42,8 +46,9 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--pages", type=int, default=256, help="pages per GPU per step")
-    ap.add_argument("--sets", type=int, default=4, help="rotating input sets (working set > L2)")
-    ap.add_argument("--e2e-steps", type=int, default=6)
+    ap.add_argument("--sets", type=int, default=4, help="input sets (rounded up to a multiple of --inflight)")
+    ap.add_argument("--inflight", type=int, default=16, help="batches in flight (CUDA streams)")
+    ap.add_argument("--e2e-steps", type=int, default=32)
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="bounded CPU baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -211,7 +216,7 @@ def ours(args):
     import torch
     import torch.distributed as dist
 
-    from ztcp_b200 import capi, codec, fused_ext, workload
+    from ztcp_b200 import capi, codec, workload
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -229,22 +234,24 @@ def ours(args):
         cpu_base = reference_baseline(args.cpu_seconds)
 
     n = args.pages
+    D = max(1, args.inflight)
+    n_sets = D * -(-max(args.sets, D) // D)  # a multiple of D: set j always runs on stream j % D
     m = workload.session_material(7)
     keys = capi.keys(*m["key"], *m["mac_key"])
     sets = []
-    for s in range(args.sets):
+    for s in range(n_sets):
         seed = 42 + 1000 * rank + s
         k, v = workload.kv_pages_torch(n, workload.GQA, seed=seed, device=dev)
-        toks = torch.from_numpy(workload.token_hashes(n, seed)).to(dev)
         sets.append({
-            "k": k, "v": v, "toks": toks,
-            "seq": (m["base_seq"] + (rank * args.sets + s) * n) % 2**64,
+            "k": k, "v": v, "toks": torch.from_numpy(workload.token_hashes(n, seed)).to(dev),
+            "seq": (m["base_seq"] + (rank * n_sets + s) * n) % 2**64,
             "blobs": torch.empty((n, BLOB_BYTES), dtype=torch.uint8, device=dev),
             "kout": torch.empty((n, 64, 8, 128), dtype=torch.float16, device=dev),
             "vout": torch.empty((n, 64, 8, 128), dtype=torch.float16, device=dev),
             "status": torch.empty(n, dtype=torch.int32, device=dev),
             "fail": torch.zeros(1, dtype=torch.int32, device=dev),
         })
+    streams = [torch.cuda.Stream(device=dev) for _ in range(D)]
 
     def egress(S):
         codec.encode_pages(S["k"], S["v"], S["toks"], S["blobs"], rope_dim=64, preset=1, rope_mode=1,
@@ -266,124 +273,165 @@ def ours(args):
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    for i in range(args.warmup):
-        S = sets[i % len(sets)]
+    def streamed(first, count, step_fn):
+        """Steps first..first+count-1 on the D streams, bracketed by events on the current stream."""
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        main = torch.cuda.current_stream(dev)
+        start.record(main)
+        for st in streams:
+            st.wait_event(start)
+        for i in range(first, first + count):
+            with torch.cuda.stream(streams[i % D]):
+                step_fn(i)
+        for st in streams:
+            done = torch.cuda.Event()
+            done.record(st)
+            main.wait_event(done)
+        end.record(main)
+        return start, end
+
+    def round_trip(i):
+        S = sets[i % n_sets]
         egress(S)
         ingress(S)
+
+    def check(what):
+        bad = sum(int(S["fail"].item()) for S in sets)
+        if bad:
+            raise RuntimeError(f"{what}: a round trip failed verification")
+
+    streamed(0, args.warmup, round_trip)
     torch.cuda.synchronize()
-    for S in sets:
-        if int(S["fail"].item()) != 0:
-            raise RuntimeError("warm-up round trip failed verification")
+    check("warm-up")
 
     K = args.steps
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(K)]
     with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
-        for i in range(K):
-            S = sets[i % len(sets)]
-            ev[i][0].record()
-            egress(S)
-            ev[i][1].record()
-            ingress(S)
-            ev[i][2].record()
+        h0 = time.perf_counter()
+        t0, t1 = streamed(args.warmup, K, round_trip)
+        host_enqueue_ms = (time.perf_counter() - h0) * 1e3
         torch.cuda.synchronize()
         barrier()
-    total_ms = ev[0][0].elapsed_time(ev[-1][2])
-    egress_ms = sum(e[0].elapsed_time(e[1]) for e in ev)
-    ingress_ms = sum(e[1].elapsed_time(e[2]) for e in ev)
-    bad = sum(int(S["fail"].item()) for S in sets)
-    if bad:
-        raise RuntimeError("a timed round trip failed verification")
+    total_ms = t0.elapsed_time(t1)
+    check("timed region")
 
+    # single-batch latency: the same round trip with one batch in flight
+    L = max(3, min(K, 8))
+    lat = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(L)]
+    for i in range(L):
+        S = sets[i % n_sets]
+        lat[i][0].record()
+        egress(S)
+        lat[i][1].record()
+        ingress(S)
+        lat[i][2].record()
     # dominant kernel (SipHash chain): verify-only launches, timed live with events
-    mac_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(K)]
-    for i in range(K):
-        S = sets[i % len(sets)]
+    mac_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(L)]
+    for i in range(L):
+        S = sets[i % n_sets]
         mac_ev[i][0].record()
         verify(S)
         mac_ev[i][1].record()
     torch.cuda.synchronize()
-    mac_ms = statistics.mean(a.elapsed_time(b) for a, b in mac_ev)
+    check("latency run")
+    egress_ms = statistics.median(e[0].elapsed_time(e[1]) for e in lat)
+    ingress_ms = statistics.median(e[1].elapsed_time(e[2]) for e in lat)
+    mac_ms = statistics.median(a.elapsed_time(b) for a, b in mac_ev)
 
-    t = torch.tensor([total_ms, egress_ms, ingress_ms, mac_ms], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, egress_ms, ingress_ms, mac_ms = (float(x) for x in t.tolist())
-
-    # end to end through the drop-in API with pinned host buffers (the reference wrapper's placement)
-    S0 = sets[0]
-    hk, hv = S0["k"].cpu().pin_memory(), S0["v"].cpu().pin_memory()
-    htoks = S0["toks"].cpu()
-    hblobs = torch.empty((n, BLOB_BYTES), dtype=torch.uint8).pin_memory()
-    hko = torch.empty((n, 64, 8, 128), dtype=torch.float16).pin_memory()
-    hvo = torch.empty_like(hko).pin_memory()
+    # end to end through the public API with pinned host buffers: every step uploads its K/V and token
+    # hashes, encodes, downloads the blobs, uploads them again, decodes, and downloads K/V and the status.
+    host = []
+    for j in range(D):
+        S = sets[j]
+        host.append({"k": S["k"].cpu().pin_memory(), "v": S["v"].cpu().pin_memory(),
+                     "toks": S["toks"].cpu().pin_memory(),
+                     "blobs": torch.empty((n, BLOB_BYTES), dtype=torch.uint8).pin_memory(),
+                     "kout": torch.empty((n, 64, 8, 128), dtype=torch.float16).pin_memory(),
+                     "vout": torch.empty((n, 64, 8, 128), dtype=torch.float16).pin_memory(),
+                     "fail": torch.zeros(1, dtype=torch.int32).pin_memory()})
 
     def e2e_step(i):
-        fused_ext.fused_encode_cold_pages_peak_into_cpu(
-            hk, hv, htoks, hblobs, 1, 1, 64, EXPECTED_PAYLOAD, m["tenant"], m["model"], m["layer"],
-            m["head_group"], (S0["seq"] + (i + 1) * 2**40) % 2**64, m["key"][0], m["key"][1], m["mac_key"][0],
-            m["mac_key"][1], m["key"][2], m["key"][3])
-        fused_ext.fused_decode_cold_pages_peak_into_cpu(
-            hblobs, htoks, hko, hvo, 64, False, m["tenant"], m["model"], m["layer"], m["key"][0], m["key"][1],
-            m["mac_key"][0], m["mac_key"][1], m["key"][2], m["key"][3])
+        H, S = host[i % D], sets[i % D]
+        S["k"].copy_(H["k"], non_blocking=True)
+        S["v"].copy_(H["v"], non_blocking=True)
+        S["toks"].copy_(H["toks"], non_blocking=True)
+        egress(S)
+        H["blobs"].copy_(S["blobs"], non_blocking=True)
+        S["blobs"].copy_(H["blobs"], non_blocking=True)
+        ingress(S)
+        H["kout"].copy_(S["kout"], non_blocking=True)
+        H["vout"].copy_(S["vout"], non_blocking=True)
+        H["fail"].copy_(S["fail"], non_blocking=True)
 
-    for i in range(2):
-        e2e_step(i)
+    E = max(D, args.e2e_steps)
+    streamed(0, D, e2e_step)
     torch.cuda.synchronize()
     barrier()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(args.e2e_steps):
-        e2e_step(i + 2)
-    e1.record()
+    e0, e1 = streamed(D, E, e2e_step)
     torch.cuda.synchronize()
-    e2e_ms = torch.tensor([e0.elapsed_time(e1) / args.e2e_steps], device=dev)
+    if any(int(H["fail"].item()) for H in host):
+        raise RuntimeError("an end-to-end round trip failed verification")
+    if not torch.equal(host[0]["kout"], sets[0]["kout"].cpu()):
+        raise RuntimeError("end-to-end output differs from the device-resident run")
+
+    t = torch.tensor([total_ms, egress_ms, ingress_ms, mac_ms, e0.elapsed_time(e1)], device=dev)
     if world > 1:
-        dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
-        barrier()
-    e2e_ms = float(e2e_ms.item())
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    total_ms, egress_ms, ingress_ms, mac_ms, e2e_total_ms = (float(x) for x in t.tolist())
 
     if rank == 0:
         hot_step = 2 * n * PAGE_HOT_BYTES * world
         wire_step = 2 * n * BLOB_BYTES * world
-        value = hot_step / (total_ms / K * 1e-3) / 1e9
+        value = hot_step * K / (total_ms * 1e-3) / 1e9
         peak, peak_kind = measured_peaks()
         mac_bytes = n * BLOB_BYTES
         achieved = mac_bytes / (mac_ms * 1e-3) / 1e9
         traffic = committed_traffic().get("mac_kernel<verify>", {}).get("dram_bytes_per_launch")
-        step_bytes = n * (PAGE_HOT_BYTES + BLOB_BYTES) * 2      # read+write, egress+ingress, one GPU
-        sm_mhz = clocks.summary()
+        clk = clocks.summary()
+        mhz = clk.get("sm_mhz") or 1965.0
+        cycles_per_word = mac_ms * 1e-3 * mhz * 1e6 / SIP_WORDS_PER_PAGE
+        step_bytes = n * (PAGE_HOT_BYTES + BLOB_BYTES) * 2 * world   # read + write, egress + ingress
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": round(total_ms / K, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, int4/int8 + fp16 scales, fp16 out",
             "data": "synthetic (seeded N(0,1), x15 RoPE outlier channels)",
             "config": {"workload": "cfg0: 256-page GQA 64x8x128 INT4_SYM+PRESERVE_FP8 egress+ingress round trip",
-                       "pages_per_gpu": n, "parallelism": f"pages sharded, {world} GPU(s), no collective",
-                       "l2": f"{args.sets} rotating input sets, {args.sets * n * (PAGE_HOT_BYTES * 2 + BLOB_BYTES) / 1e6:.0f} MB working set > 126 MB L2"},
-            "egress_gbs": round(n * world * PAGE_HOT_BYTES / (egress_ms / K * 1e-3) / 1e9, 2),
-            "ingress_gbs": round(n * world * PAGE_HOT_BYTES / (ingress_ms / K * 1e-3) / 1e9, 2),
-            "wire_gbs": round(wire_step / (total_ms / K * 1e-3) / 1e9, 2),
-            "latency_ms": {"egress": round(egress_ms / K, 4), "ingress": round(ingress_ms / K, 4)},
+                       "pages_per_gpu": n, "batches_in_flight": D,
+                       "parallelism": f"pages sharded, {world} GPU(s), no collective",
+                       "l2": f"{n_sets} input sets, {n_sets * n * (PAGE_HOT_BYTES * 2 + BLOB_BYTES) / 1e9:.2f} GB "
+                             f"working set > 126 MB L2"},
+            "wire_gbs": round(wire_step * K / (total_ms * 1e-3) / 1e9, 2),
+            "single_batch": {"egress_ms": round(egress_ms, 4), "ingress_ms": round(ingress_ms, 4),
+                             "round_trip_gbs": round(hot_step / ((egress_ms + ingress_ms) * 1e-3) / 1e9, 2),
+                             "egress_gbs": round(n * world * PAGE_HOT_BYTES / (egress_ms * 1e-3) / 1e9, 2),
+                             "ingress_gbs": round(n * world * PAGE_HOT_BYTES / (ingress_ms * 1e-3) / 1e9, 2)},
             "roofline": {"kernel": "mac_kernel<verify> (SipHash-2-4-128 chain, one lane per page)", "bound": "hbm",
                          "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 5), "traffic": traffic,
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
-                         "algorithmic_bytes_per_launch": mac_bytes, "launch_ms": round(mac_ms, 4)},
-            "path_bounds_ms": {
-                "hbm": round(step_bytes / (peak * 1e9) * 1e3, 4),
-                "chacha20_alu": round(2 * n * CHACHA_BLOCKS_PER_PAGE / 28.5e9 * 1e3, 4),
-                "siphash_alu": round(2 * n * SIP_WORDS_PER_PAGE / 410e9 * 1e3, 4),
-                "siphash_chain": round(2 * SIP_WORDS_PER_PAGE * 89.3 / ((sm_mhz.get("sm_mhz") or 1965) * 1e6) * 1e3, 4),
-                "note": "chacha20 28.5 G blocks/s, siphash 410 G words/s at full occupancy and 89.3 cycles/word per "
-                        "chain are microbenchmarked (profiles/int_alu_peaks.md)"},
-            "clocks": sm_mhz,
-            "e2e": {"value": round(hot_step / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": n * (PAGE_HOT_BYTES + BLOB_BYTES + 8 * 2),
-                    "d2h_bytes_per_step": n * (BLOB_BYTES + PAGE_HOT_BYTES),
-                    "path": "ztcp_b200.fused_ext peak_into egress + ingress, pinned host K/V/blobs, "
-                            "synchronous like the reference"},
+                         "algorithmic_bytes_per_launch": mac_bytes, "launch_ms": round(mac_ms, 4),
+                         "chain": {"cycles_per_word": round(cycles_per_word, 1), "alu_floor_cycles_per_word": 84.4,
+                                   "frac_of_alu_floor": round(84.4 / cycles_per_word, 3),
+                                   "note": "one chain = one page; ALU floor = 42.2 ALU instructions/word x 2 "
+                                           "cycles (ncu pipe counters, profiles/siphash_chain_ubench.md)"}},
+            "path_roofline": {
+                "bytes_per_step": step_bytes,
+                "hbm_bound_ms": round(step_bytes / (peak * 1e9) * 1e3, 4),
+                "alu_bound_ms": round(2 * n * (CHACHA_BLOCKS_PER_PAGE / 28.5e9 + SIP_WORDS_PER_PAGE / 410e9)
+                                      * 1e3, 4),
+                "achieved_ms_per_step": round(total_ms / K, 4),
+                "frac_hbm": round(step_bytes / (peak * 1e9) * 1e3 / (total_ms / K), 4),
+                "note": "alu bound = ChaCha20 at 28.5 G blocks/s + SipHash at 410 G words/s (microbenchmarked, "
+                        "profiles/int_alu_peaks.md); per GPU"},
+            "clocks": clk,
+            "host_enqueue_ms": round(host_enqueue_ms, 3),
+            "e2e": {"value": round(hot_step * E / (e2e_total_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": n * (PAGE_HOT_BYTES + BLOB_BYTES + 8),
+                    "d2h_bytes_per_step": n * (BLOB_BYTES + PAGE_HOT_BYTES) + 4,
+                    "path": f"ztcp_b200.codec encode_pages/decode_pages on {D} streams, pinned host K/V, "
+                            f"blobs and outputs; every step uploads its inputs and downloads blobs, K/V and status"},
             "gpu_launches": 4 * K,
         }
         if cpu_base is not None:
