@@ -37,6 +37,12 @@ BLOB_BYTES = 32 + EXPECTED_PAYLOAD + 16
 CHACHA_BLOCKS_PER_PAGE = EXPECTED_PAYLOAD // 64
 SIP_WORDS_PER_PAGE = (32 + EXPECTED_PAYLOAD) // 8 + 1
 METRIC = "egress+ingress hot-byte GB/s (INT4_SYM+PRESERVE_FP8 256-page GQA batch)"
+# Integer ceilings of the codec's primitives on B200, from vlx-tee_b200/ubench/int_peaks.cu
+# (profiles/int_alu_peaks.md): ChaCha20 blocks/s and SipHash words/s with every SM busy, and the
+# cycles/word of one chain whose input is in registers.
+CHACHA_BLOCKS_PER_S = 2.88e10
+SIP_WORDS_PER_S = 4.15e11
+REG_CHAIN_CYCLES_PER_WORD = 89.0
 
 
 def parse_args():
@@ -216,7 +222,7 @@ def ours(args):
     import torch
     import torch.distributed as dist
 
-    from ztcp_b200 import capi, codec, workload
+    from ztcp_b200 import capi, codec, sharding, workload
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -244,7 +250,7 @@ def ours(args):
         k, v = workload.kv_pages_torch(n, workload.GQA, seed=seed, device=dev)
         sets.append({
             "k": k, "v": v, "toks": torch.from_numpy(workload.token_hashes(n, seed)).to(dev),
-            "seq": (m["base_seq"] + (rank * n_sets + s) * n) % 2**64,
+            "seq": (m["base_seq"] + sharding.global_page_base(rank, s, n_sets, n)) % 2**64,
             "blobs": torch.empty((n, BLOB_BYTES), dtype=torch.uint8, device=dev),
             "kout": torch.empty((n, 64, 8, 128), dtype=torch.float16, device=dev),
             "vout": torch.empty((n, 64, 8, 128), dtype=torch.float16, device=dev),
@@ -375,10 +381,8 @@ def ours(args):
     if not torch.equal(host[0]["kout"], sets[0]["kout"].cpu()):
         raise RuntimeError("end-to-end output differs from the device-resident run")
 
-    t = torch.tensor([total_ms, egress_ms, ingress_ms, mac_ms, e0.elapsed_time(e1)], device=dev)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    total_ms, egress_ms, ingress_ms, mac_ms, e2e_total_ms = (float(x) for x in t.tolist())
+    total_ms, egress_ms, ingress_ms, mac_ms, e2e_total_ms = sharding.max_over_ranks(
+        [total_ms, egress_ms, ingress_ms, mac_ms, e0.elapsed_time(e1)], device=dev)
 
     if rank == 0:
         hot_step = 2 * n * PAGE_HOT_BYTES * world
@@ -412,19 +416,20 @@ def ours(args):
                          "frac": round(achieved / peak, 5), "traffic": traffic,
                          "peak_source": f"MEASURED_PEAKS.json hbm_gbs ({peak_kind})",
                          "algorithmic_bytes_per_launch": mac_bytes, "launch_ms": round(mac_ms, 4),
-                         "chain": {"cycles_per_word": round(cycles_per_word, 1), "alu_floor_cycles_per_word": 84.4,
-                                   "frac_of_alu_floor": round(84.4 / cycles_per_word, 3),
-                                   "note": "one chain = one page; ALU floor = 42.2 ALU instructions/word x 2 "
-                                           "cycles (ncu pipe counters, profiles/siphash_chain_ubench.md)"}},
+                         "chain": {"cycles_per_word": round(cycles_per_word, 1),
+                                   "register_chain_cycles_per_word": REG_CHAIN_CYCLES_PER_WORD,
+                                   "frac_of_register_chain": round(REG_CHAIN_CYCLES_PER_WORD / cycles_per_word, 3),
+                                   "note": "one chain = one page; the floor is the same SipHash code with its input in "
+                                           "registers, ALU-pipe bound (profiles/int_alu_peaks.md)"}},
             "path_roofline": {
                 "bytes_per_step": step_bytes,
                 "hbm_bound_ms": round(step_bytes / (peak * 1e9) * 1e3, 4),
-                "alu_bound_ms": round(2 * n * (CHACHA_BLOCKS_PER_PAGE / 28.5e9 + SIP_WORDS_PER_PAGE / 410e9)
-                                      * 1e3, 4),
+                "alu_bound_ms": round(2 * n * (CHACHA_BLOCKS_PER_PAGE / CHACHA_BLOCKS_PER_S
+                                               + SIP_WORDS_PER_PAGE / SIP_WORDS_PER_S) * 1e3, 4),
                 "achieved_ms_per_step": round(total_ms / K, 4),
                 "frac_hbm": round(step_bytes / (peak * 1e9) * 1e3 / (total_ms / K), 4),
-                "note": "alu bound = ChaCha20 at 28.5 G blocks/s + SipHash at 410 G words/s (microbenchmarked, "
-                        "profiles/int_alu_peaks.md); per GPU"},
+                "note": "alu bound = ChaCha20 keystream at its all-SM rate + SipHash words at the all-SM chain "
+                        "rate (profiles/int_alu_peaks.md); per GPU"},
             "clocks": clk,
             "host_enqueue_ms": round(host_enqueue_ms, 3),
             "e2e": {"value": round(hot_step * E / (e2e_total_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
