@@ -48,13 +48,18 @@ REG_CHAIN_CYCLES_PER_WORD = 89.0
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=256,
+                    help="timed steps (one 256-page round trip each); the pipeline needs a few times --inflight "
+                         "steps to reach steady state")
+    ap.add_argument("--warmup", type=int, default=8)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--pages", type=int, default=256, help="pages per GPU per step")
     ap.add_argument("--sets", type=int, default=4, help="input sets (rounded up to a multiple of --inflight)")
-    ap.add_argument("--inflight", type=int, default=16, help="batches in flight (CUDA streams)")
+    ap.add_argument("--inflight", type=int, default=32, help="batches in flight (CUDA streams)")
     ap.add_argument("--e2e-steps", type=int, default=32)
+    ap.add_argument("--e2e-inflight", type=int, default=8,
+                    help="batches in flight in the end-to-end run (host<->device copies are link-bound; a few "
+                         "streams keep both copy directions busy)")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="bounded CPU baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -279,17 +284,19 @@ def ours(args):
         if world > 1:
             dist.barrier(device_ids=[local])
 
-    def streamed(first, count, step_fn):
-        """Steps first..first+count-1 on the D streams, bracketed by events on the current stream."""
+    def streamed(first, count, step_fn, pool=None):
+        """Steps first..first+count-1 round-robin on `pool` (default: the D streams), bracketed by events on
+        the current stream."""
+        pool = streams if pool is None else pool
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         main = torch.cuda.current_stream(dev)
         start.record(main)
-        for st in streams:
+        for st in pool:
             st.wait_event(start)
         for i in range(first, first + count):
-            with torch.cuda.stream(streams[i % D]):
+            with torch.cuda.stream(pool[i % len(pool)]):
                 step_fn(i)
-        for st in streams:
+        for st in pool:
             done = torch.cuda.Event()
             done.record(st)
             main.wait_event(done)
@@ -347,8 +354,10 @@ def ours(args):
 
     # end to end through the public API with pinned host buffers: every step uploads its K/V and token
     # hashes, encodes, downloads the blobs, uploads them again, decodes, and downloads K/V and the status.
+    DE = max(1, min(args.e2e_inflight, n_sets))
+    e2e_streams = streams[:DE]
     host = []
-    for j in range(D):
+    for j in range(DE):
         S = sets[j]
         host.append({"k": S["k"].cpu().pin_memory(), "v": S["v"].cpu().pin_memory(),
                      "toks": S["toks"].cpu().pin_memory(),
@@ -358,7 +367,7 @@ def ours(args):
                      "fail": torch.zeros(1, dtype=torch.int32).pin_memory()})
 
     def e2e_step(i):
-        H, S = host[i % D], sets[i % D]
+        H, S = host[i % DE], sets[i % DE]
         S["k"].copy_(H["k"], non_blocking=True)
         S["v"].copy_(H["v"], non_blocking=True)
         S["toks"].copy_(H["toks"], non_blocking=True)
@@ -370,11 +379,11 @@ def ours(args):
         H["vout"].copy_(S["vout"], non_blocking=True)
         H["fail"].copy_(S["fail"], non_blocking=True)
 
-    E = max(D, args.e2e_steps)
-    streamed(0, D, e2e_step)
+    E = max(4 * DE, args.e2e_steps)
+    streamed(0, DE, e2e_step, e2e_streams)
     torch.cuda.synchronize()
     barrier()
-    e0, e1 = streamed(D, E, e2e_step)
+    e0, e1 = streamed(DE, E, e2e_step, e2e_streams)
     torch.cuda.synchronize()
     if any(int(H["fail"].item()) for H in host):
         raise RuntimeError("an end-to-end round trip failed verification")
@@ -435,7 +444,7 @@ def ours(args):
             "e2e": {"value": round(hot_step * E / (e2e_total_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": n * (PAGE_HOT_BYTES + BLOB_BYTES + 8),
                     "d2h_bytes_per_step": n * (BLOB_BYTES + PAGE_HOT_BYTES) + 4,
-                    "path": f"ztcp_b200.codec encode_pages/decode_pages on {D} streams, pinned host K/V, "
+                    "path": f"ztcp_b200.codec encode_pages/decode_pages on {DE} streams, {E} steps, pinned host K/V, "
                             f"blobs and outputs; every step uploads its inputs and downloads blobs, K/V and status"},
             "gpu_launches": 4 * K,
         }

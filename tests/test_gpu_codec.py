@@ -347,3 +347,50 @@ def test_rounding_ties_match_oracle(ext, oracle, preset, rope_mode):
                        exp, m)
     want = helpers.oracle_encode(oracle, k, v, toks, 0, preset, rope_mode, exp, m)
     np.testing.assert_array_equal(blobs.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("T,H,D,rope", [(40, 2, 48, 16), (64, 8, 128, 64), (24, 4, 64, 0), (16, 8, 96, 32),
+                                        (64, 1, 576, 64)])
+def test_aligned_geometries_every_layout(ext, oracle, T, H, D, rope):
+    """16-byte aligned blobs and regions on every preset x rope mode: tiles that do not divide the page,
+    regions that start inside a 64-byte keystream block, bf16 and fp16 input, and edge values (inf, +-65504,
+    values whose scale is subnormal) mixed into N(0,1) data."""
+    from ztcp_b200 import workload
+
+    rng = np.random.default_rng(T * 7 + D)
+    edge = np.array([np.inf, -np.inf, 65504, -65504, 1e-7, -3e-6, 0.0, -0.0], dtype=np.float32)
+
+    def page_values(shape):
+        x = rng.standard_normal(shape).astype(np.float32)
+        mask = rng.random(shape) < 0.03
+        x[mask] = rng.choice(edge, int(mask.sum()))
+        tiny = rng.random(shape[:3]) < 0.05  # whole rows of tiny values: subnormal scales
+        x[tiny] *= 1e-6
+        return x
+
+    for preset in (1, 2, 3):
+        for rope_mode in (0, 1, 2):
+            for mla in ((True,) if D == 576 else (False, True)):
+                for bf16 in (False, True):
+                    k32 = page_values((3, T, H, D))
+                    v32 = None if mla else page_values((3, T, H, D))
+                    if bf16:
+                        kt = torch.from_numpy(k32).to(torch.bfloat16)
+                        vt = None if v32 is None else torch.from_numpy(v32).to(torch.bfloat16)
+                        k16, v16 = kt.half().numpy(), None if vt is None else vt.half().numpy()
+                    else:
+                        k16, v16 = k32.astype(np.float16), None if v32 is None else v32.astype(np.float16)
+                        kt, vt = torch.from_numpy(k16), None if v16 is None else torch.from_numpy(v16)
+                    m = workload.session_material(int(rng.integers(1 << 30)))
+                    toks = workload.token_hashes(3, int(rng.integers(1 << 30)))
+                    exp = (oracle.spec_payload_bytes(preset, rope_mode, T * H, D, rope, not mla) + 15) // 16 * 16
+                    blobs = gpu_encode(ext, kt, vt, torch.from_numpy(toks), rope, preset, rope_mode, exp, m)
+                    want = helpers.oracle_encode(oracle, k16, v16, toks, rope, preset, rope_mode, exp, m)
+                    tag = f"T{T} H{H} D{D} rope{rope} preset{preset} mode{rope_mode} mla{mla} bf16{bf16}"
+                    np.testing.assert_array_equal(blobs.cpu().numpy(), want, err_msg=tag)
+                    kd, vd = gpu_decode(ext, blobs, torch.from_numpy(toks), k16.shape, rope, mla, m)
+                    okd, ovd, _, first = helpers.oracle_decode(oracle, want, toks, k16.shape, rope, mla, m)
+                    assert first == -1
+                    np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd, err_msg=tag)
+                    if not mla:
+                        np.testing.assert_array_equal(vd.cpu().numpy().view(np.uint16), ovd, err_msg=tag)

@@ -142,6 +142,10 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
   P.n_tiles = (int32_t)((vecs + P.tile_vecs - 1) / P.tile_vecs);
   P.n_pages = batch->n_pages;
   P.stage_bytes = ztcp::plan_stage(P.L, P.tile_vecs, P.stage_q, P.stage_s);
+  for (int i = 0; i < 3; ++i) {
+    const int64_t groups = i < P.L.n ? P.L.sec[i].dim / ztcp::kGroup : 0;
+    P.gshift[i] = (groups > 0 && (groups & (groups - 1)) == 0) ? __builtin_ctzll(groups) : -1;
+  }
   if (P.stage_bytes > kMaxStageBytes) return fail(ZTCP_EINVAL, "head_dim too large for one tile");
   if (P.n_pages * P.n_tiles > 0x7FFFFFFFLL) return fail(ZTCP_EINVAL, "batch too large for one launch");
   cudaStream_t s = static_cast<cudaStream_t>(stream);

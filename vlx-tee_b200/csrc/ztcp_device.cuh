@@ -182,25 +182,28 @@ __device__ __forceinline__ uint32_t group_amax_bits(const uint32_t w[8]) {
 // Exact scalar quantizers (the reference's x86 semantics, including NaN products); used for groups
 // whose scale is subnormal, zero or non-finite, or that hold a non-finite element.
 // ------------------------------------------------------------------------------------------------
-__device__ __forceinline__ float f16_at(const uint32_t w[8], int i) {
+__device__ __forceinline__ float f16_at(const uint32_t* w, int i) {
   return f16_bits_to_f32((i & 1) ? hi16(w[i >> 1]) : lo16(w[i >> 1]));
 }
 
-// amax with a 1e-6 floor; NaN elements never compare greater (csrc:737-744 / 808-815)
-__device__ __forceinline__ float group_amax_exact(const uint32_t w[8]) {
+// amax of NW fp16x2 words with a 1e-6 floor; NaN elements never compare greater (csrc:737-744 /
+// 808-815)
+template <int NW>
+__device__ __forceinline__ float amax_exact(const uint32_t* w) {
   float amax = 1e-6f;
 #pragma unroll
-  for (int i = 0; i < 16; ++i) {
+  for (int i = 0; i < 2 * NW; ++i) {
     const float av = fabsf(f16_at(w, i));
     amax = av > amax ? av : amax;
   }
   return amax;
 }
 
-// INT8: q = clamp(rint(x * inv), -127, 127); a NaN product quantizes to +127.
-__device__ __forceinline__ void quant_int8_exact(const uint32_t w[8], float inv, uint32_t q[4]) {
+// INT8: q = clamp(rint(x * inv), -127, 127); a NaN product quantizes to +127.  NQ output words.
+template <int NQ>
+__device__ __forceinline__ void quant_int8_exact(const uint32_t* w, float inv, uint32_t* q) {
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < NQ; ++k) {
     uint32_t word = 0;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -213,10 +216,12 @@ __device__ __forceinline__ void quant_int8_exact(const uint32_t w[8], float inv,
   }
 }
 
-// INT4: u = clamp(int(rint(x * inv) + 8), 0, 15) with x86 float->int conversion (NaN -> 0).
-__device__ __forceinline__ void quant_int4_exact(const uint32_t w[8], float inv, uint32_t q[2]) {
+// INT4: u = clamp(int(rint(x * inv) + 8), 0, 15) with x86 float->int conversion (NaN -> 0).  NQ output
+// words.
+template <int NQ>
+__device__ __forceinline__ void quant_int4_exact(const uint32_t* w, float inv, uint32_t* q) {
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
+  for (int k = 0; k < NQ; ++k) {
     uint32_t word = 0;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -249,7 +254,7 @@ __device__ __forceinline__ uint32_t round_bits(float x, float inv) {
 __device__ __forceinline__ bool group_scale(const uint32_t w[8], float rq, __half* sh, float* inv) {
   const uint32_t amax_bits = group_amax_bits(w);
   if (amax_bits >= 0x7C00u) {  // inf or NaN element: exact path computes everything
-    *sh = __float2half_rn(__fmul_rn(group_amax_exact(w), rq));
+    *sh = __float2half_rn(__fmul_rn(amax_exact<8>(w), rq));
     *inv = __frcp_rn(__half2float(*sh));
     return false;
   }
@@ -263,7 +268,7 @@ __device__ __forceinline__ uint16_t quant_int8(const uint32_t w[8], uint32_t q[4
   __half sh;
   float inv;
   if (!group_scale(w, 1.0f / 127.0f, &sh, &inv)) {
-    quant_int8_exact(w, inv, q);
+    quant_int8_exact<4>(w, inv, q);
     return __half_as_ushort(sh);
   }
 #pragma unroll
@@ -281,20 +286,21 @@ __device__ __forceinline__ uint16_t quant_int4(const uint32_t w[8], uint32_t q[2
   __half sh;
   float inv;
   if (!group_scale(w, 1.0f / 7.0f, &sh, &inv)) {
-    quant_int4_exact(w, inv, q);
+    quant_int4_exact<2>(w, inv, q);
     return __half_as_ushort(sh);
   }
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
-    uint32_t acc = 0;
+    uint32_t b[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[4 * k + j]));
-      // nibble = rint(p) mod 16; +8 is applied to all eight nibbles at once below (flip bit 3)
-      acc |= (round_bits(x.x, inv) & 0xFu) << (8 * j);
-      acc |= (round_bits(x.y, inv) & 0xFu) << (8 * j + 4);
+      // low byte = nibble(e0) | nibble(e1) << 4, nibble = rint(p) mod 16 (the +8 comes below)
+      const uint32_t lo = round_bits(x.x, inv), hi = round_bits(x.y, inv) << 4;
+      b[j] = (lo & 0x0Fu) | (hi & 0xF0u);
     }
-    q[k] = acc ^ 0x88888888u;
+    // bytes 0..3 of the word; +8 on all eight nibbles at once (flip bit 3: q + 8 in 4-bit two's complement)
+    q[k] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410) ^ 0x88888888u;
   }
   return __half_as_ushort(sh);
 }
@@ -312,10 +318,12 @@ __device__ __forceinline__ uint16_t dequant_one(float q, float s) {
   return __half_as_ushort(__float2half_rn(p));
 }
 
-__device__ __forceinline__ void dequant_exact(const uint32_t* q, int bits, uint16_t scale, uint32_t out[8]) {
+// NOUT output words (2 * NOUT elements).
+template <int NOUT>
+__device__ __forceinline__ void dequant_exact(const uint32_t* q, int bits, uint16_t scale, uint32_t* out) {
   const float s = f16_bits_to_f32(scale);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
+  for (int i = 0; i < NOUT; ++i) {
     float a, b;
     if (bits == 8) {
       const uint32_t w = q[i / 2] >> (16 * (i & 1));
@@ -333,15 +341,17 @@ __device__ __forceinline__ void dequant_exact(const uint32_t* q, int bits, uint1
 __device__ __forceinline__ uint32_t h2_bits(__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); }
 __device__ __forceinline__ __half2 bits_h2(uint32_t u) { return *reinterpret_cast<const __half2*>(&u); }
 
-__device__ __forceinline__ void dequant_int8(const uint32_t q[4], uint16_t scale, uint32_t out[8]) {
+// NQ q words (4 elements each) -> 2 * NQ output words.
+template <int NQ>
+__device__ __forceinline__ void dequant_int8(const uint32_t* q, uint16_t scale, uint32_t* out) {
   if ((scale & 0x7C00u) == 0x7C00u) {
-    dequant_exact(q, 8, scale, out);
+    dequant_exact<2 * NQ>(q, 8, scale, out);
     return;
   }
   const __half2 s2 = __half2half2(__ushort_as_half(scale));
   const __half2 bias = __float2half2_rn(1152.0f);  // 0x6400 | (q ^ 0x80) = 1152 + q
 #pragma unroll
-  for (int k = 0; k < 4; ++k) {
+  for (int k = 0; k < NQ; ++k) {
     const uint32_t u = q[k] ^ 0x80808080u;
     const uint32_t lo = __byte_perm(u, 0x64646464u, 0x5140), hi = __byte_perm(u, 0x64646464u, 0x7362);
     out[2 * k] = h2_bits(__hmul2_rn(__hsub2(bits_h2(lo), bias), s2));
@@ -349,15 +359,17 @@ __device__ __forceinline__ void dequant_int8(const uint32_t q[4], uint16_t scale
   }
 }
 
-__device__ __forceinline__ void dequant_int4(const uint32_t q[2], uint16_t scale, uint32_t out[8]) {
+// NQ q words (8 elements each) -> 4 * NQ output words.
+template <int NQ>
+__device__ __forceinline__ void dequant_int4(const uint32_t* q, uint16_t scale, uint32_t* out) {
   if ((scale & 0x7C00u) == 0x7C00u) {
-    dequant_exact(q, 4, scale, out);
+    dequant_exact<4 * NQ>(q, 4, scale, out);
     return;
   }
   const __half2 s2 = __half2half2(__ushort_as_half(scale));
   const __half2 bias = __float2half2_rn(1032.0f);  // 0x6400 | u = 1024 + u, q = u - 8
 #pragma unroll
-  for (int k = 0; k < 2; ++k) {
+  for (int k = 0; k < NQ; ++k) {
     const uint32_t w = q[k];  // nibbles e0..e7 of this word, element i at bits 4i
     // (e0,e4) (e1,e5) (e2,e6) (e3,e7) as fp16 pairs 1024 + u
     const uint32_t p0 = (w & 0x000F000Fu) | 0x64006400u;

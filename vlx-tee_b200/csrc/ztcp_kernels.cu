@@ -102,6 +102,90 @@ __device__ __forceinline__ void xor_block_bytes(uint8_t* dst, const uint8_t* src
   }
 }
 
+// One section's slice of a tile: source rows, staging areas and the (vec, group) index split.
+struct SectionTile {
+  const uint16_t* src;  // first source element of the tile's first row in this section
+  uint8_t* q;           // staging of the q (or raw) region for the tile
+  uint8_t* sc;          // staging of the scale region for the tile
+  int32_t row_stride;   // elements between rows (head_dim)
+  int32_t q_bpv, s_bpv; // staging bytes per vec
+  int32_t groups;       // 16-element groups per row in this section
+  int32_t gshift;       // log2(groups), or -1 when groups is not a power of two
+  int32_t tv;           // vecs in this tile
+};
+
+__device__ __forceinline__ void split_item(int it, const SectionTile& t, int& vec, int& g) {
+  if (t.gshift >= 0) {
+    vec = it >> t.gshift;
+    g = it & (t.groups - 1);
+  } else {
+    vec = it / t.groups;
+    g = it - vec * t.groups;
+  }
+}
+
+template <int KIND, bool BF16>
+__device__ __forceinline__ void quantize_section(const SectionTile& t) {
+  const int items = t.tv * t.groups;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    int vec, g;
+    split_item(it, t, vec, g);
+    uint32_t w[8];
+    load_group16<BF16>(t.src + vec * t.row_stride + g * 16, w);
+    uint8_t* qd = t.q + vec * t.q_bpv;
+    if (KIND == kRaw) {
+      uint4* d = reinterpret_cast<uint4*>(qd + g * 32);
+      d[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      d[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    } else if (KIND == kInt8) {
+      uint32_t q[4];
+      const uint16_t sc = quant_int8(w, q);
+      *reinterpret_cast<uint4*>(qd + g * 16) = make_uint4(q[0], q[1], q[2], q[3]);
+      *reinterpret_cast<uint16_t*>(t.sc + vec * t.s_bpv + g * 2) = sc;
+    } else {
+      uint32_t q[2];
+      const uint16_t sc = quant_int4(w, q);
+      *reinterpret_cast<uint2*>(qd + g * 8) = make_uint2(q[0], q[1]);
+      *reinterpret_cast<uint16_t*>(t.sc + vec * t.s_bpv + g * 2) = sc;
+    }
+  }
+}
+
+// Dequantize one section's slice of a tile from staging into the KV pool rows.
+template <int KIND>
+__device__ __forceinline__ void dequantize_section(const SectionTile& t, uint16_t* dst) {
+  const int items = t.tv * t.groups;
+  for (int it = threadIdx.x; it < items; it += blockDim.x) {
+    int vec, g;
+    split_item(it, t, vec, g);
+    uint4* d = reinterpret_cast<uint4*>(dst + vec * t.row_stride + g * 16);
+    const uint8_t* qs = t.q + vec * t.q_bpv;
+    if (KIND == kRaw) {
+      const uint4* q = reinterpret_cast<const uint4*>(qs + g * 32);
+      d[0] = q[0];
+      d[1] = q[1];
+      continue;
+    }
+    const uint16_t scale = *reinterpret_cast<const uint16_t*>(t.sc + vec * t.s_bpv + g * 2);
+    uint32_t o[8];
+    if (KIND == kInt8) {
+      const uint4 q = *reinterpret_cast<const uint4*>(qs + g * 16);
+      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+      dequant_int8<4>(qw, scale, o);
+    } else {
+      const uint2 q = *reinterpret_cast<const uint2*>(qs + g * 8);
+      const uint32_t qw[2] = {q.x, q.y};
+      dequant_int4<2>(qw, scale, o);
+    }
+    d[0] = make_uint4(o[0], o[1], o[2], o[3]);
+    d[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+__device__ __forceinline__ int32_t log2_if_pow2(int32_t x) {
+  return (x > 0 && (x & (x - 1)) == 0) ? __ffs(x) - 1 : -1;
+}
+
 // ------------------------------------------------------------------------------------------------
 // Egress: quantize + pack + encrypt one (page, vec-tile)
 // ------------------------------------------------------------------------------------------------
@@ -120,40 +204,15 @@ __global__ void __launch_bounds__(kTileThreads) egress_tile_kernel(const __grid_
   const uint16_t* vp = P.v ? P.v + blk * P.page_elems : nullptr;
 
   // ---- phase 1: quantize this tile's rows of every section into shared memory
-  int items[3] = {0, 0, 0};
-  int total = 0;
 #pragma unroll
-  for (int s = 0; s < 3; ++s)
-    if (s < P.L.n) {
-      items[s] = tv * (pick(P.L, s).dim >> 4);
-      total += items[s];
-    }
-  for (int it = threadIdx.x; it < total; it += blockDim.x) {
-    int s = 0, local = it;
-    if (local >= items[0]) { local -= items[0]; s = 1; if (local >= items[1]) { local -= items[1]; s = 2; } }
-    const Section S = pick(P.L, s);
-    const int groups = S.dim >> 4;
-    const int vec = local / groups, g = local - vec * groups;
-    const uint16_t* src = (S.buf ? vp : kp) + (v0 + vec) * P.head_dim + S.col + g * 16;
-    uint32_t w[8];
-    load_group16<BF16>(src, w);
-    uint8_t* qd = stage + (s == 0 ? P.stage_q[0] : (s == 1 ? P.stage_q[1] : P.stage_q[2])) + vec * S.q_bpv;
-    uint8_t* sd = stage + (s == 0 ? P.stage_s[0] : (s == 1 ? P.stage_s[1] : P.stage_s[2])) + vec * S.s_bpv;
-    if (S.kind == kRaw) {
-      uint4* d = reinterpret_cast<uint4*>(qd + g * 32);
-      d[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      d[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    } else if (S.kind == kInt8) {
-      uint32_t q[4];
-      const uint16_t sc = quant_int8(w, q);
-      *reinterpret_cast<uint4*>(qd + g * 16) = make_uint4(q[0], q[1], q[2], q[3]);
-      *reinterpret_cast<uint16_t*>(sd + g * 2) = sc;
-    } else {
-      uint32_t q[2];
-      const uint16_t sc = quant_int4(w, q);
-      *reinterpret_cast<uint2*>(qd + g * 8) = make_uint2(q[0], q[1]);
-      *reinterpret_cast<uint16_t*>(sd + g * 2) = sc;
-    }
+  for (int s = 0; s < 3; ++s) {
+    if (s >= P.L.n) break;
+    const Section S = P.L.sec[s];
+    const SectionTile st{(S.buf ? vp : kp) + v0 * P.head_dim + S.col, stage + P.stage_q[s], stage + P.stage_s[s],
+                         P.head_dim, S.q_bpv, S.s_bpv, S.dim >> 4, P.gshift[s], tv};
+    if (S.kind == kInt4) quantize_section<kInt4, BF16>(st);
+    else if (S.kind == kInt8) quantize_section<kInt8, BF16>(st);
+    else quantize_section<kRaw, BF16>(st);
   }
 
   // header (32 bytes) by tile 0
@@ -450,40 +509,17 @@ __global__ void __launch_bounds__(kTileThreads) ingress_tile_kernel(const __grid
   __syncthreads();
 
   // ---- phase 2: dequantize into the paged KV layout
-  int items[3] = {0, 0, 0};
-  int total = 0;
 #pragma unroll
-  for (int s = 0; s < 3; ++s)
-    if (s < L.n) {
-      items[s] = tv * (pick(L, s).dim >> 4);
-      total += items[s];
-    }
-  for (int it = threadIdx.x; it < total; it += blockDim.x) {
-    int s = 0, local = it;
-    if (local >= items[0]) { local -= items[0]; s = 1; if (local >= items[1]) { local -= items[1]; s = 2; } }
-    const Section S = pick(L, s);
-    const int groups = S.dim >> 4;
-    const int vec = local / groups, g = local - vec * groups;
-    uint4* dst = reinterpret_cast<uint4*>((S.buf ? vd : kd) + (v0 + vec) * P.head_dim + S.col + g * 16);
-    const uint8_t* qs = stage + s_sq[s] + vec * S.q_bpv;
-    const uint8_t* sc = stage + s_ss[s] + vec * S.s_bpv + g * 2;
-    uint32_t o[8];
-    if (S.kind == kRaw) {
-      const uint4* q = reinterpret_cast<const uint4*>(qs + g * 32);
-      dst[0] = q[0];
-      dst[1] = q[1];
-      continue;
-    } else if (S.kind == kInt8) {
-      const uint4 q = *reinterpret_cast<const uint4*>(qs + g * 16);
-      const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
-      dequant_int8(qw, *reinterpret_cast<const uint16_t*>(sc), o);
-    } else {
-      const uint2 q = *reinterpret_cast<const uint2*>(qs + g * 8);
-      const uint32_t qw[2] = {q.x, q.y};
-      dequant_int4(qw, *reinterpret_cast<const uint16_t*>(sc), o);
-    }
-    dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
-    dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+  for (int s = 0; s < 3; ++s) {
+    if (s >= L.n) break;
+    const Section S = L.sec[s];
+    const int32_t groups = S.dim >> 4;
+    const SectionTile st{nullptr, stage + s_sq[s], stage + s_ss[s], P.head_dim, S.q_bpv, S.s_bpv, groups,
+                         log2_if_pow2(groups), tv};
+    uint16_t* dst = (S.buf ? vd : kd) + v0 * P.head_dim + S.col;
+    if (S.kind == kInt4) dequantize_section<kInt4>(st, dst);
+    else if (S.kind == kInt8) dequantize_section<kInt8>(st, dst);
+    else dequantize_section<kRaw>(st, dst);
   }
 }
 

@@ -40,6 +40,7 @@ struct EgressParams {
   int64_t n_pages;
   int32_t stage_q[3];       // shared-memory staging offsets (bytes) for a full tile
   int32_t stage_s[3];
+  int32_t gshift[3];        // log2(groups per row) of each section, -1 when not a power of two
   int32_t stage_bytes;
 };
 
