@@ -62,6 +62,10 @@ def parse_args():
                          "streams keep both copy directions busy)")
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="bounded CPU baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--prefix-pages", type=int, default=4096,
+                    help="BASELINE config 4: pages of the full-prefix sweep, split over the ranks (0 = skip)")
+    ap.add_argument("--prefix-chunk", type=int, default=256, help="pages per launch in the prefix sweep")
+    ap.add_argument("--prefix-reps", type=int, default=3)
     return ap.parse_args()
 
 
@@ -224,6 +228,7 @@ def reference_arm(args):
 # our arm
 # ------------------------------------------------------------------------------------------------
 def ours(args):
+    import numpy as np
     import torch
     import torch.distributed as dist
 
@@ -390,8 +395,67 @@ def ours(args):
     if not torch.equal(host[0]["kout"], sets[0]["kout"].cpu()):
         raise RuntimeError("end-to-end output differs from the device-resident run")
 
+    # a 4,096-page prefix (64 layers x 64 pages) addressed through a seeded shuffled
+    # block-table list, split into contiguous shards over the ranks (strong scaling).  Each rank holds only
+    # its own blocks; egress of the whole shard, then ingress, for INT4_SYM and K8V4_ASYM, in chunks of
+    # --prefix-chunk pages over the streams.
+    prefix = None
+    if args.prefix_pages > 0:
+        P = args.prefix_pages
+        p0, pc = sharding.shard_range(P, world, rank)
+        order = np.random.default_rng(4096).permutation(P)          # list position -> global block id
+        mine = order[p0:p0 + pc]
+        slot = {int(b): i for i, b in enumerate(np.sort(mine))}    # global block id -> local pool slot
+        table = torch.tensor([slot[int(b)] for b in mine], dtype=torch.int32, device=dev)
+        pk, pv = workload.kv_pages_torch(pc, workload.GQA, seed=4242 + rank, device=dev)
+        ptoks = torch.from_numpy(workload.token_hashes(P, 4096)[p0:p0 + pc].copy()).to(dev)
+        pseq = torch.tensor([(m["base_seq"] + (1 << 40) + p0 + i) % 2**64 for i in range(pc)],
+                            dtype=torch.uint64).to(dev)
+        pko = torch.empty((pc, 64, 8, 128), dtype=torch.float16, device=dev)
+        pvo = torch.empty_like(pko)
+        pst = torch.empty(pc, dtype=torch.int32, device=dev)
+        chunks = [(a, min(a + args.prefix_chunk, pc)) for a in range(0, pc, args.prefix_chunk)]
+        pfail = torch.zeros(max(1, len(chunks)), dtype=torch.int32, device=dev)
+        pool = streams[:max(1, min(len(chunks), len(streams)))]
+        prefix = {}
+        for name, preset, payload in (("int4_sym", 1, EXPECTED_PAYLOAD), ("k8v4_asym", 2, 114688)):
+            pblobs = torch.empty((pc, 48 + payload), dtype=torch.uint8, device=dev)
+
+            def p_egress(ci, preset=preset, payload=payload, pblobs=pblobs):
+                a, b = chunks[ci]
+                codec.encode_pages(pk, pv, ptoks[a:b], pblobs[a:b], rope_dim=64, preset=preset, rope_mode=1,
+                                   expected_payload_bytes=payload, tenant_id_hash=m["tenant"],
+                                   model_id_hash=m["model"], layer_id=m["layer"], head_group_id=m["head_group"],
+                                   base_sequence_nonce=0, keys=keys, block_table=table[a:b],
+                                   sequence_nonces=pseq[a:b], check_block_table=False)
+
+            def p_ingress(ci, pblobs=pblobs):
+                a, b = chunks[ci]
+                codec.decode_pages(pblobs[a:b], ptoks[a:b], pko, pvo, rope_dim=64, is_mla=False,
+                                   tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"],
+                                   keys=keys, block_table=table[a:b], status=pst[a:b], any_fail=pfail[ci:ci + 1],
+                                   check_block_table=False)
+
+            t_e, t_i = [], []
+            for rep in range(1 + args.prefix_reps):
+                barrier()
+                torch.cuda.synchronize()
+                a0, a1 = streamed(0, len(chunks), p_egress, pool)
+                b0, b1 = streamed(0, len(chunks), p_ingress, pool)
+                torch.cuda.synchronize()
+                if int(pfail.sum().item()):
+                    raise RuntimeError("prefix sweep: a page failed verification")
+                if rep:
+                    t_e.append(a0.elapsed_time(a1))
+                    t_i.append(b0.elapsed_time(b1))
+            prefix[name] = (statistics.median(t_e), statistics.median(t_i), payload)
+            del pblobs
+
     total_ms, egress_ms, ingress_ms, mac_ms, e2e_total_ms = sharding.max_over_ranks(
         [total_ms, egress_ms, ingress_ms, mac_ms, e0.elapsed_time(e1)], device=dev)
+    if prefix is not None:
+        flat = sharding.max_over_ranks([x for nm in prefix for x in prefix[nm][:2]], device=dev)
+        prefix = {nm: (flat[2 * j], flat[2 * j + 1], prefix[nm][2]) for j, nm in enumerate(prefix)}
 
     if rank == 0:
         hot_step = 2 * n * PAGE_HOT_BYTES * world
@@ -448,6 +512,21 @@ def ours(args):
                             f"blobs and outputs; every step uploads its inputs and downloads blobs, K/V and status"},
             "gpu_launches": 4 * K,
         }
+        if prefix is not None:
+            P = args.prefix_pages
+            sweep = {"workload": f"cfg4: {P}-page prefix (64 layers x 64 pages of 64x8x128 GQA K+V bf16), seeded "
+                                 f"shuffled block table, contiguous shards over {world} GPU(s), {args.prefix_chunk}-page "
+                                 f"launches on up to {len(pool)} streams per GPU",
+                     "pages_total": P, "pages_per_gpu": -(-P // world), "hot_bytes": P * PAGE_HOT_BYTES}
+            for nm, (te, ti, payload) in prefix.items():
+                sweep[nm] = {"egress_ms": round(te, 4), "ingress_ms": round(ti, 4),
+                             "egress_hot_gbs": round(P * PAGE_HOT_BYTES / (te * 1e-3) / 1e9, 2),
+                             "ingress_hot_gbs": round(P * PAGE_HOT_BYTES / (ti * 1e-3) / 1e9, 2),
+                             "round_trip_hot_gbs": round(2 * P * PAGE_HOT_BYTES / ((te + ti) * 1e-3) / 1e9, 2),
+                             "wire_gbs": round(2 * P * (48 + payload) / ((te + ti) * 1e-3) / 1e9, 2)}
+            sweep["note"] = ("strong scaling is bounded below by one page's tag chain per direction "
+                             f"(~{mac_ms:.2f} ms measured): per-GPU time cannot fall under it however few pages a GPU holds")
+            line["prefix_sweep"] = sweep
         if cpu_base is not None:
             line["cpu_baseline"] = cpu_base
         print(json.dumps(line))

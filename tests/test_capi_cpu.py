@@ -11,7 +11,9 @@ import pytest
 from ztcp_b200 import build, capi
 from ztcp_b200.cold_page_spec import ColdPageAAD, ColdPageGeometry, QuantPreset, RoPEMode
 
-HEADER = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include", "ztcp_b200.h")
+INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+HEADER = os.path.join(INCLUDE, "ztcp_b200.h")
+LEDGER_HEADER = os.path.join(INCLUDE, "ztcp_ledger.h")
 
 
 @pytest.fixture(scope="module")
@@ -20,15 +22,19 @@ def lib():
     return capi.load()
 
 
-def declared_functions():
-    text = open(HEADER).read()
+def declared_functions(path=HEADER):
+    text = open(path).read()
     return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(ztcp_\w+)\(", text, re.M)))
 
 
 def test_exports_every_declared_symbol(lib):
+    from ztcp_b200 import ledger
+
     names = declared_functions()
     assert set(names) == set(capi.EXPORTED_SYMBOLS)
-    for n in names:
+    ledger_names = declared_functions(LEDGER_HEADER)
+    assert set(ledger_names) == set(ledger.LEDGER_SYMBOLS)
+    for n in names + ledger_names:
         assert hasattr(lib, n), n
     assert lib.ztcp_version() >= 100
 

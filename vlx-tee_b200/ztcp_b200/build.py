@@ -1,6 +1,6 @@
 """Build recipe for libztcp_b200.so (sm_100a).
 
-Compiles the CUDA sources in ``vlx-tee_b200/csrc`` with nvcc into
+Compiles the CUDA and host C++ sources in ``vlx-tee_b200/csrc`` with nvcc into
 ``vlx-tee_b200/ztcp_b200/libztcp_b200.so``, in-tree, so the built library
 travels with the repository to GPU machines.  nvcc cross-compiles for sm_100a
 without a GPU present.
@@ -25,12 +25,12 @@ NVCC_FLAGS = [
 
 
 def sources() -> list[str]:
-    return sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    return sorted(glob.glob(os.path.join(CSRC, "*.cu")) + glob.glob(os.path.join(CSRC, "*.cpp")))
 
 
 def _inputs() -> list[str]:
     return sources() + sorted(glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh"))) + [
-        os.path.join(INCLUDE, "ztcp_b200.h")
+        os.path.join(INCLUDE, "ztcp_b200.h"), os.path.join(INCLUDE, "ztcp_ledger.h")
     ]
 
 
