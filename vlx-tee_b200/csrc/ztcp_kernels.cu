@@ -189,8 +189,9 @@ __device__ __forceinline__ int32_t log2_if_pow2(int32_t x) {
 // ------------------------------------------------------------------------------------------------
 // Egress: quantize + pack + encrypt one (page, vec-tile)
 // ------------------------------------------------------------------------------------------------
+// 7 resident CTAs per SM (the register cap this implies was measured ~5 % faster than 6).
 template <bool BF16>
-__global__ void __launch_bounds__(kTileThreads) egress_tile_kernel(const __grid_constant__ EgressParams P) {
+__global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __grid_constant__ EgressParams P) {
   extern __shared__ __align__(16) uint8_t stage[];
   __shared__ RangeTable T;
   const int64_t page = blockIdx.x / P.n_tiles;
@@ -434,7 +435,8 @@ __global__ void __launch_bounds__(kChainThreads, 1) mac_kernel(const __grid_cons
 // ------------------------------------------------------------------------------------------------
 // Ingress: decrypt + dequantize one (page, vec-tile), or zero it when the batch failed
 // ------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(kTileThreads) ingress_tile_kernel(const __grid_constant__ IngressParams P) {
+// 6 resident CTAs per SM (measured ~9 % faster than the 5 its unconstrained register count allows).
+__global__ void __launch_bounds__(kTileThreads, 6) ingress_tile_kernel(const __grid_constant__ IngressParams P) {
   extern __shared__ __align__(16) uint8_t stage[];
   const int64_t page = blockIdx.x / P.n_tiles;
   const int tile = (int)(blockIdx.x - page * P.n_tiles);
