@@ -250,6 +250,13 @@ int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_g
   // worst case over every (preset, rope_mode) a header may carry, plus 16-byte rounding per area
   if (P.tile_vecs * worst + 6 * 16 > kMaxStageBytes) return fail(ZTCP_EINVAL, "head_dim too large for one tile");
   P.stage_bytes = (int32_t)(P.tile_vecs * worst + 6 * 16);
+  // layouts and staging plans of every flags byte a verified header may carry
+  for (int p = 1; p <= 3; ++p)
+    for (int r = 0; r <= 2; ++r) {
+      const int i = (p - 1) * 3 + r;
+      ztcp::build_layout(p, r, vecs, geom->head_dim, geom->rope_dim, has_v, &P.lay[i]);
+      ztcp::plan_stage(P.lay[i], P.tile_vecs, P.lay_q[i], P.lay_s[i]);
+    }
   if (P.n_pages * P.n_tiles > 0x7FFFFFFFLL) return fail(ZTCP_EINVAL, "batch too large for one launch");
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -457,47 +457,52 @@ __global__ void __launch_bounds__(kTileThreads, 6) ingress_tile_kernel(const __g
     return;
   }
 
+  // header: the flags byte selects the page's layout from the host-built table; nonce words for the
+  // keystream (seq lo, seq hi, layer_id << 16 | head_group_id)
   const uint8_t* blob = P.blobs + page * P.blob_stride;
   __shared__ RangeTable T;
-  __shared__ Layout sL;
-  __shared__ int32_t s_sq[3], s_ss[3];
-  __shared__ uint32_t s_n0, s_n1, s_n2;
-  if (threadIdx.x == 0) {
-    const uint8_t flags = blob[3];
-    const uint32_t layer_hg = ld_u32_any(blob + 12);
-    s_n0 = ld_u32_any(blob + 24);                  // sequence_nonce low word
-    s_n1 = ld_u32_any(blob + 28);                  // sequence_nonce high word
-    s_n2 = (layer_hg << 16) | (layer_hg >> 16);    // layer_id << 16 | head_group_id
-    build_layout(flags & 0x0F, (flags >> 4) & 0x0F, P.vecs, P.head_dim, P.rope_dim, P.has_v != 0, &sL);
-    plan_stage(sL, P.tile_vecs, s_sq, s_ss);
-    build_range_table(T, sL, v0, tv, s_sq, s_ss, false, P.payload_len);
+  uint32_t h0, h3, h6, h7;
+  if ((reinterpret_cast<uintptr_t>(blob) & 15) == 0) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(blob));
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(blob) + 1);
+    h0 = a.x; h3 = a.w; h6 = b.z; h7 = b.w;
+  } else {
+    h0 = ld_u32_any(blob); h3 = ld_u32_any(blob + 12); h6 = ld_u32_any(blob + 24); h7 = ld_u32_any(blob + 28);
   }
+  const uint32_t flags = h0 >> 24;
+  const int li = (int)((flags & 0x0Fu) - 1u) * 3 + (int)((flags >> 4) & 0x0Fu);
+  const Layout& L = P.lay[li];
+  const int32_t* sq = P.lay_q[li];
+  const int32_t* ss = P.lay_s[li];
+  if (threadIdx.x == 0) build_range_table(T, L, v0, tv, sq, ss, false, P.payload_len);
   __syncthreads();
-  const Layout& L = sL;
 
-  // ---- phase 1: decrypt this tile's byte ranges into shared memory
+  // ---- phase 1: decrypt this tile's byte ranges into shared memory (loads issued before the keystream)
   const int64_t total_blocks = T.first[T.n];
-  const uint32_t n0 = s_n0, n1 = s_n1, n2 = s_n2;
+  const uint32_t n0 = h6, n1 = h7, n2 = (h3 << 16) | (h3 >> 16);
   const uint8_t* payload = blob + kHeaderBytes;
   for (int64_t bi = threadIdx.x; bi < total_blocks; bi += blockDim.x) {
     const int i = find_range(T, bi);
     const Range r = T.r[i];
     const int64_t kb = (r.a >> 6) + (bi - T.first[i]);
     uint32_t ks[16];
-    chacha20_block(P.key, (uint32_t)(1 + kb), n0, n1, n2, ks);
     const int64_t base = kb << 6;
     const int lo = (int)(max(r.a, base) - base), hi = (int)(min(r.b, base + 64) - base);
     const uint8_t* src = payload + base;
     uint8_t* dst = stage + r.stage + (base - r.a);  // only bytes [lo, hi) are written
     if (lo == 0 && hi == 64 &&
         ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+      uint4 c[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) c[w] = __ldg(reinterpret_cast<const uint4*>(src) + w);
+      chacha20_block(P.key, (uint32_t)(1 + kb), n0, n1, n2, ks);
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
-        uint4 c = __ldg(reinterpret_cast<const uint4*>(src) + w);
-        c.x ^= ks[4 * w]; c.y ^= ks[4 * w + 1]; c.z ^= ks[4 * w + 2]; c.w ^= ks[4 * w + 3];
-        reinterpret_cast<uint4*>(dst)[w] = c;
+        c[w].x ^= ks[4 * w]; c[w].y ^= ks[4 * w + 1]; c[w].z ^= ks[4 * w + 2]; c[w].w ^= ks[4 * w + 3];
+        reinterpret_cast<uint4*>(dst)[w] = c[w];
       }
     } else {
+      chacha20_block(P.key, (uint32_t)(1 + kb), n0, n1, n2, ks);
 #pragma unroll
       for (int w = 0; w < 16; ++w) {
 #pragma unroll
@@ -516,7 +521,7 @@ __global__ void __launch_bounds__(kTileThreads, 6) ingress_tile_kernel(const __g
     if (s >= L.n) break;
     const Section S = L.sec[s];
     const int32_t groups = S.dim >> 4;
-    const SectionTile st{nullptr, stage + s_sq[s], stage + s_ss[s], P.head_dim, S.q_bpv, S.s_bpv, groups,
+    const SectionTile st{nullptr, stage + sq[s], stage + ss[s], P.head_dim, S.q_bpv, S.s_bpv, groups,
                          log2_if_pow2(groups), tv};
     uint16_t* dst = (S.buf ? vd : kd) + v0 * P.head_dim + S.col;
     if (S.kind == kInt4) dequantize_section<kInt4>(st, dst);

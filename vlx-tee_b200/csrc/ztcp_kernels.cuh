@@ -78,6 +78,11 @@ struct IngressParams {
   int32_t n_tiles;
   int64_t n_pages;
   int32_t stage_bytes;
+  // layout and staging plan of every valid header flags byte, indexed by (preset - 1) * 3 + rope_mode
+  // (every page reaching the decrypt pass has been verified, so its flags select a valid entry)
+  Layout lay[9];
+  int32_t lay_q[9][3];
+  int32_t lay_s[9][3];
 };
 
 void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream);
