@@ -37,6 +37,7 @@ BLOB_BYTES = 32 + EXPECTED_PAYLOAD + 16
 CHACHA_BLOCKS_PER_PAGE = EXPECTED_PAYLOAD // 64
 SIP_WORDS_PER_PAGE = (32 + EXPECTED_PAYLOAD) // 8 + 1
 METRIC = "egress+ingress hot-byte GB/s (INT4_SYM+PRESERVE_FP8 256-page GQA batch)"
+WORKLOAD = "cfg0: 256-page GQA 64x8x128 INT4_SYM+PRESERVE_FP8 egress+ingress round trip"
 # Integer ceilings of the codec's primitives on B200, from vlx-tee_b200/ubench/int_peaks.cu
 # (profiles/int_alu_peaks.md): ChaCha20 blocks/s and SipHash words/s with every SM busy, and the
 # cycles/word of one chain whose input is in registers.
@@ -157,8 +158,13 @@ class ClockSampler:
 # reference codec on the host cores
 # ------------------------------------------------------------------------------------------------
 def _ref_worker(args):
-    """One process: the reference's peak egress + peak ingress on `pages` pages until `seconds` pass."""
+    """One process: the reference's peak egress + peak ingress on `pages` pages until `seconds` pass.
+
+    Runs the reference codec built from its own source (oracle/_ref); where that build is absent, the
+    oracle's C restatement of it (same work per page, kind "port").  Returns (pages, seconds, kind)."""
     worker, pages, seconds = args
+    import numpy as np
+
     sys.path.insert(0, os.path.join(REPO, "oracle"))
     sys.path.insert(0, os.path.join(REPO, "vlx-tee_b200"))
     import torch
@@ -167,29 +173,51 @@ def _ref_worker(args):
     from ztcp_b200 import workload
 
     torch.set_num_threads(1)
-    ref = build_ref.load_module()
     k32, v32 = workload.kv_pages_np(pages, workload.GQA, seed=42 + worker)
     k = torch.from_numpy(k32).to(torch.bfloat16).half()   # the reference codec accepts fp16 only
     v = torch.from_numpy(v32).to(torch.bfloat16).half()
     m = workload.session_material(7)
     toks = torch.from_numpy(workload.token_hashes(pages, 11 + worker))
-    out = torch.empty((pages, BLOB_BYTES), dtype=torch.uint8)
-    kd, vd = torch.empty_like(k), torch.empty_like(v)
     key, mk = m["key"], m["mac_key"]
+    try:
+        ref = build_ref.load_module()
+    except FileNotFoundError:
+        ref = None
+    if ref is None:
+        import ztcp_oracle as port
+
+        kb, vb, tk = k.numpy().view(np.uint16), v.numpy().view(np.uint16), toks.numpy()
+
+        def round_trip(it):
+            blobs = port.encode_batch(kb, vb, tk, rope_dim=64, preset=1, rope_mode=1,
+                                      expected_payload=EXPECTED_PAYLOAD, tenant=m["tenant"], model=m["model"],
+                                      layer=m["layer"], head_group=m["head_group"],
+                                      base_seq=(m["base_seq"] + it * pages + worker * 2**32) % 2**64, key=key,
+                                      mac_key=mk)
+            port.decode_batch(blobs, tk, num_tokens=64, num_heads=8, head_dim=128, rope_dim=64, is_mla=False,
+                              tenant=m["tenant"], model=m["model"], layer=m["layer"], key=key, mac_key=mk)
+        kind = "port"
+    else:
+        out = torch.empty((pages, BLOB_BYTES), dtype=torch.uint8)
+        kd, vd = torch.empty_like(k), torch.empty_like(v)
+
+        def round_trip(it):
+            ref.fused_encode_cold_pages_peak_into_cpu(k, v, toks, out, 1, 1, 64, EXPECTED_PAYLOAD, m["tenant"],
+                                                      m["model"], m["layer"], m["head_group"],
+                                                      (m["base_seq"] + it * pages + worker * 2**32) % 2**64,
+                                                      key[0], key[1], mk[0], mk[1], key[2], key[3])
+            ref.fused_decode_cold_pages_peak_into_cpu(out, toks, kd, vd, 64, False, m["tenant"], m["model"],
+                                                      m["layer"], key[0], key[1], mk[0], mk[1], key[2], key[3])
+        kind = "reference"
     done, it = 0, 0
     t0 = time.perf_counter()
     while True:
-        ref.fused_encode_cold_pages_peak_into_cpu(k, v, toks, out, 1, 1, 64, EXPECTED_PAYLOAD, m["tenant"],
-                                                  m["model"], m["layer"], m["head_group"],
-                                                  (m["base_seq"] + it * pages + worker * 2**32) % 2**64,
-                                                  key[0], key[1], mk[0], mk[1], key[2], key[3])
-        ref.fused_decode_cold_pages_peak_into_cpu(out, toks, kd, vd, 64, False, m["tenant"], m["model"], m["layer"],
-                                                  key[0], key[1], mk[0], mk[1], key[2], key[3])
+        round_trip(it)
         done += pages
         it += 1
         el = time.perf_counter() - t0
         if el >= seconds:
-            return done, el
+            return done, el, kind
 
 
 def reference_baseline(seconds: float, pages_per_worker: int = 8):
@@ -201,11 +229,15 @@ def reference_baseline(seconds: float, pages_per_worker: int = 8):
         res = pool.map(_ref_worker, [(w, pages_per_worker, seconds) for w in range(cores)])
     pages = sum(r[0] for r in res)
     wall = max(r[1] for r in res)
+    kind = res[0][2]
     gbs = 2 * pages * PAGE_HOT_BYTES / wall / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
-            "sample": (f"{cores} processes x {pages_per_worker}-page batches for {seconds:.0f} s: reference "
-                       f"fused_encode_cold_pages_peak_into_cpu + fused_decode_cold_pages_peak_into_cpu "
-                       f"(oracle/_ref, scalar x86-64 build, 1 thread each); {pages} pages round-tripped")}
+    what = ("reference fused_encode_cold_pages_peak_into_cpu + fused_decode_cold_pages_peak_into_cpu (oracle/_ref, "
+            "the reference's own source, scalar x86-64 build, 1 thread each)" if kind == "reference" else
+            "the oracle's C restatement of the reference codec, batch encode + decode (oracle/_ref absent), "
+            "1 thread each")
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": kind,
+            "sample": (f"{cores} processes x {pages_per_worker}-page batches for {seconds:g} s: {what}; "
+                       f"{pages} pages round-tripped")}
 
 
 def reference_arm(args):
@@ -217,8 +249,7 @@ def reference_arm(args):
     line = {"metric": METRIC, "value": base["value"], "unit": "GB/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
-            "config": {"workload": "cfg0: 256-page GQA 64x8x128 INT4_SYM+PRESERVE_FP8 egress+ingress",
-                       "pages": args.pages, "host_cores": base["cores"]},
+            "config": {"workload": WORKLOAD, "pages_per_gpu": args.pages, "host_cores": base["cores"]},
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
@@ -474,7 +505,7 @@ def ours(args):
             "warmup": args.warmup, "ms_per_step": round(total_ms / K, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, int4/int8 + fp16 scales, fp16 out",
             "data": "synthetic (seeded N(0,1), x15 RoPE outlier channels)",
-            "config": {"workload": "cfg0: 256-page GQA 64x8x128 INT4_SYM+PRESERVE_FP8 egress+ingress round trip",
+            "config": {"workload": WORKLOAD,
                        "pages_per_gpu": n, "batches_in_flight": D,
                        "parallelism": f"pages sharded, {world} GPU(s), no collective",
                        "l2": f"{n_sets} input sets, {n_sets * n * (PAGE_HOT_BYTES * 2 + BLOB_BYTES) / 1e9:.2f} GB "
