@@ -263,7 +263,7 @@ def ours(args):
     import torch
     import torch.distributed as dist
 
-    from ztcp_b200 import capi, codec, sharding, workload
+    from ztcp_b200 import capi, codec, offload, sharding, workload
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -391,7 +391,6 @@ def ours(args):
     # end to end through the public API with pinned host buffers: every step uploads its K/V and token
     # hashes, encodes, downloads the blobs, uploads them again, decodes, and downloads K/V and the status.
     DE = max(1, min(args.e2e_inflight, n_sets))
-    e2e_streams = streams[:DE]
     host = []
     for j in range(DE):
         S = sets[j]
@@ -400,29 +399,43 @@ def ours(args):
                      "blobs": torch.empty((n, BLOB_BYTES), dtype=torch.uint8).pin_memory(),
                      "kout": torch.empty((n, 64, 8, 128), dtype=torch.float16).pin_memory(),
                      "vout": torch.empty((n, 64, 8, 128), dtype=torch.float16).pin_memory(),
-                     "fail": torch.zeros(1, dtype=torch.int32).pin_memory()})
+                     })
+
+    # through ztcp_b200.offload.OffloadPipeline: each step's egress (upload K/V -> encode -> download blobs) and
+    # ingress (upload blobs -> decode -> download K/V + status) on the pipeline's slots; a step's egress waits
+    # for the ingress that last used the same host buffers.
+    pipe = offload.OffloadPipeline(dev, slots=2 * DE)
+    last_ingress = [None] * DE
 
     def e2e_step(i):
         H, S = host[i % DE], sets[i % DE]
-        S["k"].copy_(H["k"], non_blocking=True)
-        S["v"].copy_(H["v"], non_blocking=True)
-        S["toks"].copy_(H["toks"], non_blocking=True)
-        egress(S)
-        H["blobs"].copy_(S["blobs"], non_blocking=True)
-        S["blobs"].copy_(H["blobs"], non_blocking=True)
-        ingress(S)
-        H["kout"].copy_(S["kout"], non_blocking=True)
-        H["vout"].copy_(S["vout"], non_blocking=True)
-        H["fail"].copy_(S["fail"], non_blocking=True)
+        t = pipe.egress(H["k"], H["v"], H["toks"], H["blobs"], rope_dim=64, preset=1, rope_mode=1,
+                        expected_payload_bytes=EXPECTED_PAYLOAD, tenant_id_hash=m["tenant"], model_id_hash=m["model"],
+                        layer_id=m["layer"], head_group_id=m["head_group"], base_sequence_nonce=S["seq"], keys=keys,
+                        after=last_ingress[i % DE])
+        last_ingress[i % DE] = pipe.ingress(H["blobs"], H["toks"], H["kout"], H["vout"], rope_dim=64, is_mla=False,
+                                            tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"],
+                                            keys=keys, after=t)
 
     E = max(4 * DE, args.e2e_steps)
-    streamed(0, DE, e2e_step, e2e_streams)
+    for i in range(DE):
+        e2e_step(i)
+    for tk in last_ingress:
+        tk.wait()
     torch.cuda.synchronize()
     barrier()
-    e0, e1 = streamed(DE, E, e2e_step, e2e_streams)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for sl in pipe._slots:
+        sl.stream.wait_event(e0)
+    for i in range(DE, DE + E):
+        e2e_step(i)
+    for sl in pipe._slots:
+        torch.cuda.current_stream(dev).wait_event(sl.idle)
+    e1.record()
     torch.cuda.synchronize()
-    if any(int(H["fail"].item()) for H in host):
-        raise RuntimeError("an end-to-end round trip failed verification")
+    for tk in last_ingress:
+        tk.wait()  # raises the reference's error if any page failed
     if not torch.equal(host[0]["kout"], sets[0]["kout"].cpu()):
         raise RuntimeError("end-to-end output differs from the device-resident run")
 
@@ -539,8 +552,9 @@ def ours(args):
             "e2e": {"value": round(hot_step * E / (e2e_total_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "h2d_bytes_per_step": n * (PAGE_HOT_BYTES + BLOB_BYTES + 8),
                     "d2h_bytes_per_step": n * (BLOB_BYTES + PAGE_HOT_BYTES) + 4,
-                    "path": f"ztcp_b200.codec encode_pages/decode_pages on {DE} streams, {E} steps, pinned host K/V, "
-                            f"blobs and outputs; every step uploads its inputs and downloads blobs, K/V and status"},
+                    "path": f"ztcp_b200.offload.OffloadPipeline ({2 * DE} slots, {DE} host buffer sets), {E} steps, "
+                            f"pinned host K/V, blobs and outputs; every step uploads its K/V and token hashes, "
+                            f"encodes, downloads the blobs, uploads them again, decodes, downloads K/V and status"},
             "gpu_launches": 4 * K,
         }
         if prefix is not None:

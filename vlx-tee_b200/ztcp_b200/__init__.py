@@ -6,6 +6,7 @@ Modules:
   fused_ext      -- drop-in for the reference's native module (NativeCppFusedColdPageCodec._ext)
   cold_page_spec -- wire-format spec mirror (header, presets, geometry, payload sizes)
   session        -- GPU-native session codec: the reference wrapper's six methods on CUDA tensors
+  offload        -- egress to / ingress from pinned host memory with copies overlapped across slots
   keyring        -- session keyring with the reference's interface, per-page tables in the C++ ledger
   ledger         -- ctypes binding of the ledger C-ABI (include/ztcp_ledger.h)
   errors         -- exception classes with the reference's names and hierarchy
@@ -15,5 +16,5 @@ Modules:
 """
 from . import build, capi, cold_page_spec  # noqa: F401
 
-__all__ = ["build", "capi", "cold_page_spec", "codec", "errors", "fused_ext", "keyring", "ledger", "session",
-           "sharding", "workload"]
+__all__ = ["build", "capi", "cold_page_spec", "codec", "errors", "fused_ext", "keyring", "ledger", "offload",
+           "session", "sharding", "workload"]
