@@ -394,3 +394,34 @@ def test_aligned_geometries_every_layout(ext, oracle, T, H, D, rope):
                     np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd, err_msg=tag)
                     if not mla:
                         np.testing.assert_array_equal(vd.cpu().numpy().view(np.uint16), ovd, err_msg=tag)
+
+
+@pytest.mark.parametrize("preset,rope_mode", [(1, 0), (3, 0), (2, 1)])
+def test_bf16_groups_at_the_fp16_boundary(ext, oracle, preset, rope_mode):
+    """bf16 input quantized without the fp16 round trip: groups whose amax sits just below, at and above
+    the direct path's thresholds (2^-9 for INT4, 2^-5 for INT8) and that also hold values below fp16's
+    normal range, values fp16 rounds (subnormal) and values past 65504 -- bytes equal the fp16 path's."""
+    from ztcp_b200 import workload
+
+    rng = np.random.default_rng(preset * 10 + rope_mode)
+    T, H, D = 16, 2, 64
+    n = 2 * T * H * D // 16
+    amaxes = np.array([2.0**-9 * f for f in (0.99, 1.0, 1.01)] + [2.0**-5 * f for f in (0.99, 1.0, 1.01)]
+                      + [1.0, 300.0, 6.5e4, 7.0e4], dtype=np.float32)
+    tiny = np.array([2.0**-15, -2.0**-20, 3.1e-6, 2.0**-14, -6.0e-8, 0.0], dtype=np.float32)
+    groups = []
+    for i in range(n):
+        g = rng.uniform(-1, 1, 16).astype(np.float32) * amaxes[i % len(amaxes)] * 0.9
+        g[rng.integers(0, 16)] = amaxes[i % len(amaxes)] * (1 if i % 2 else -1)
+        for j in rng.choice(16, 4, replace=False):
+            g[j] = tiny[rng.integers(0, len(tiny))]
+        groups.append(g)
+    x = np.stack(groups).reshape(2, 1, T, H, D)
+    kb = torch.from_numpy(x[0]).to(torch.bfloat16)
+    vb = torch.from_numpy(x[1]).to(torch.bfloat16)
+    m = workload.session_material(71)
+    toks = workload.token_hashes(1, 72)
+    exp = oracle.spec_payload_bytes(preset, rope_mode, T * H, D, 16, True)
+    blobs = gpu_encode(ext, kb, vb, torch.from_numpy(toks), 16, preset, rope_mode, exp, m)
+    want = helpers.oracle_encode(oracle, kb.half().numpy(), vb.half().numpy(), toks, 16, preset, rope_mode, exp, m)
+    np.testing.assert_array_equal(blobs.cpu().numpy(), want)

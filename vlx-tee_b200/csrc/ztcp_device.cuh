@@ -306,6 +306,55 @@ __device__ __forceinline__ uint16_t quant_int4(const uint32_t w[8], uint32_t q[2
 }
 
 // ------------------------------------------------------------------------------------------------
+// bf16 input without the round trip through fp16.  A bf16 value in fp16's normal range converts to
+// fp16 exactly, so only elements below 2^-14 (or above 65504) could change.  With the group amax in
+// [2^-9, 65280] (INT4) or [2^-5, 65280] (INT8) -- at least 4 * qmax * 2^-14 -- every element below
+// 2^-14 has |x * inv| < 0.26 and quantizes to 0 from either value, and the amax is itself an exact fp16
+// value, so the scale and every q equal the fp16 path's.  Other groups convert and take that path.
+// ------------------------------------------------------------------------------------------------
+constexpr uint32_t kBf16MaxFp16 = 0x477Fu;  // largest bf16 <= 65504
+
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+
+// true when the direct path applied; w holds raw bf16 pairs
+__device__ __forceinline__ bool quant_int4_bf16(const uint32_t w[8], uint32_t q[2], uint16_t* scale) {
+  const uint32_t ab = group_amax_bits(w);
+  if (ab < 0x3B00u || ab > kBf16MaxFp16) return false;
+  const __half sh = __float2half_rn(__fmul_rn(__uint_as_float(ab << 16), 1.0f / 7.0f));
+  const float inv = __frcp_rn(__half2float(sh));
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    uint32_t b[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t x = w[4 * k + j];
+      const uint32_t lo = round_bits(bf16_lo(x), inv), hi = round_bits(bf16_hi(x), inv) << 4;
+      b[j] = (lo & 0x0Fu) | (hi & 0xF0u);
+    }
+    q[k] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410) ^ 0x88888888u;
+  }
+  *scale = __half_as_ushort(sh);
+  return true;
+}
+
+__device__ __forceinline__ bool quant_int8_bf16(const uint32_t w[8], uint32_t q[4], uint16_t* scale) {
+  const uint32_t ab = group_amax_bits(w);
+  if (ab < 0x3D00u || ab > kBf16MaxFp16) return false;
+  const __half sh = __float2half_rn(__fmul_rn(__uint_as_float(ab << 16), 1.0f / 127.0f));
+  const float inv = __frcp_rn(__half2float(sh));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const uint32_t a = w[2 * k], b = w[2 * k + 1];
+    const uint32_t ab2 = __byte_perm(round_bits(bf16_lo(a), inv), round_bits(bf16_hi(a), inv), 0x0040);
+    const uint32_t cd = __byte_perm(round_bits(bf16_lo(b), inv), round_bits(bf16_hi(b), inv), 0x0040);
+    q[k] = __byte_perm(ab2, cd, 0x5410);
+  }
+  *scale = __half_as_ushort(sh);
+  return true;
+}
+
+// ------------------------------------------------------------------------------------------------
 // Dequantizers: fp16(float(q) * float(scale)).  float(q) * float(scale) is exact in fp32 (<= 8 + 11
 // significant bits), so one IEEE half multiply of half(q) by the scale rounds it identically; half(q)
 // is built exactly as (1024 + u) - bias from the bit pattern 0x6400 | u.  A non-finite scale takes the

@@ -131,20 +131,38 @@ __device__ __forceinline__ void quantize_section(const SectionTile& t) {
     int vec, g;
     split_item(it, t, vec, g);
     uint32_t w[8];
-    load_group16<BF16>(t.src + vec * t.row_stride + g * 16, w);
+    load_group16<false>(t.src + vec * t.row_stride + g * 16, w);  // raw bits
     uint8_t* qd = t.q + vec * t.q_bpv;
     if (KIND == kRaw) {
+      if (BF16) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
+      }
       uint4* d = reinterpret_cast<uint4*>(qd + g * 32);
       d[0] = make_uint4(w[0], w[1], w[2], w[3]);
       d[1] = make_uint4(w[4], w[5], w[6], w[7]);
     } else if (KIND == kInt8) {
       uint32_t q[4];
-      const uint16_t sc = quant_int8(w, q);
+      uint16_t sc;
+      if (!BF16 || !quant_int8_bf16(w, q, &sc)) {
+        if (BF16) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
+        }
+        sc = quant_int8(w, q);
+      }
       *reinterpret_cast<uint4*>(qd + g * 16) = make_uint4(q[0], q[1], q[2], q[3]);
       *reinterpret_cast<uint16_t*>(t.sc + vec * t.s_bpv + g * 2) = sc;
     } else {
       uint32_t q[2];
-      const uint16_t sc = quant_int4(w, q);
+      uint16_t sc;
+      if (!BF16 || !quant_int4_bf16(w, q, &sc)) {
+        if (BF16) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
+        }
+        sc = quant_int4(w, q);
+      }
       *reinterpret_cast<uint2*>(qd + g * 8) = make_uint2(q[0], q[1]);
       *reinterpret_cast<uint16_t*>(t.sc + vec * t.s_bpv + g * 2) = sc;
     }
