@@ -139,6 +139,14 @@ int32_t ztcp_chacha20_xor(const uint8_t* src, uint8_t* dst, int64_t len, const u
 int32_t ztcp_siphash24_128(const uint8_t* src, int64_t len, uint64_t mk0, uint64_t mk1, uint8_t* out16,
                            void* stream);
 
+/* Peer gather of blobs encoded on several GPUs into one buffer on `dst_device` (the offload path's
+ * "one sender" step; the reference has no GPU, this has no reference counterpart): part i
+ * (`bytes[i]` bytes at `srcs[i]` on `src_devices[i]`) lands at dst + bytes[0] + ... + bytes[i-1].  One
+ * cudaMemcpyPeerAsync per part, enqueued on `stream` (a stream of dst_device): copy-engine transfers,
+ * no kernel reads another GPU's memory. */
+int32_t ztcp_gather(uint8_t* dst, int32_t dst_device, const uint8_t* const* srcs, const int32_t* src_devices,
+                    const int64_t* bytes, int32_t n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

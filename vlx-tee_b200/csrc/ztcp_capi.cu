@@ -286,4 +286,19 @@ int32_t ztcp_siphash24_128(const uint8_t* src, int64_t len, uint64_t mk0, uint64
   return launch_status("siphash_kernel");
 }
 
+int32_t ztcp_gather(uint8_t* dst, int32_t dst_device, const uint8_t* const* srcs, const int32_t* src_devices,
+                    const int64_t* bytes, int32_t n, void* stream) {
+  if (n < 0 || (n > 0 && (!dst || !srcs || !src_devices || !bytes))) return fail(ZTCP_EINVAL, "gather arguments must not be NULL");
+  int64_t off = 0;
+  for (int32_t i = 0; i < n; ++i) {
+    if (bytes[i] < 0 || (bytes[i] > 0 && !srcs[i])) return fail(ZTCP_EINVAL, "gather part sizes must be non-negative");
+    if (bytes[i] == 0) continue;
+    const cudaError_t e = cudaMemcpyPeerAsync(dst + off, dst_device, srcs[i], src_devices[i], (size_t)bytes[i],
+                                              static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return fail(ZTCP_ECUDA, std::string("cudaMemcpyPeerAsync: ") + cudaGetErrorString(e));
+    off += bytes[i];
+  }
+  return ZTCP_OK;
+}
+
 }  // extern "C"

@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "ztcp_verify_pages",
     "ztcp_chacha20_xor",
     "ztcp_siphash24_128",
+    "ztcp_gather",
 )
 
 
@@ -112,6 +113,8 @@ def load() -> C.CDLL:
     L.ztcp_chacha20_xor.argtypes = [vp, vp, i64, C.c_char_p, u32, C.c_char_p, vp]
     L.ztcp_siphash24_128.restype = i32
     L.ztcp_siphash24_128.argtypes = [vp, i64, u64, u64, vp, vp]
+    L.ztcp_gather.restype = i32
+    L.ztcp_gather.argtypes = [vp, i32, C.POINTER(vp), C.POINTER(i32), C.POINTER(i64), i32, vp]
     _lib = L
     return L
 

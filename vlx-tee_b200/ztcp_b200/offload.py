@@ -17,6 +17,8 @@ from __future__ import annotations
 
 import torch
 
+import ctypes as C
+
 from . import capi, codec
 
 
@@ -137,3 +139,29 @@ class OffloadPipeline:
     def synchronize(self) -> None:
         for s in self._slots:
             s.idle.synchronize()
+
+
+def gather(parts: list[torch.Tensor], device: torch.device | str) -> torch.Tensor:
+    """Concatenate uint8 blob tensors that live on several GPUs into one [sum of rows, blob_bytes] tensor
+    on `device`, with one peer copy (copy engine, cudaMemcpyPeerAsync) per part on the current stream of
+    `device`.  All parts must have the same row width."""
+    dev = torch.device(device)
+    if dev.type != "cuda" or not parts:
+        raise RuntimeError("gather needs CUDA parts and a CUDA destination")
+    width = parts[0].shape[1]
+    for p in parts:
+        if p.device.type != "cuda" or p.dtype != torch.uint8 or p.dim() != 2 or p.shape[1] != width:
+            raise RuntimeError("gather parts must be 2-D uint8 CUDA tensors of one row width")
+    parts = [p.contiguous() for p in parts]
+    out = torch.empty((sum(p.shape[0] for p in parts), width), dtype=torch.uint8, device=dev)
+    n = len(parts)
+    srcs = (C.c_void_p * n)(*[p.data_ptr() for p in parts])
+    devs = (C.c_int32 * n)(*[p.device.index for p in parts])
+    sizes = (C.c_int64 * n)(*[p.numel() for p in parts])
+    for p in parts:  # the copies start once each part's producer (its own device's current stream) is done
+        torch.cuda.current_stream(dev).wait_stream(torch.cuda.current_stream(p.device))
+    with torch.cuda.device(dev):
+        rc = capi.load().ztcp_gather(C.c_void_p(out.data_ptr()), dev.index, srcs, devs, sizes, n,
+                                     C.c_void_p(torch.cuda.current_stream(dev).cuda_stream))
+    capi.check(rc)
+    return out
