@@ -69,7 +69,10 @@ typedef struct ztcp_keys {
  *   seq nonce    sequence_nonce[i]  (device uint64; NULL = base_sequence_nonce + i, csrc:1994)
  *   layer id     layer_id[i]        (device uint16; NULL = layer_id_uniform)
  * tenant / model hash and head group are shared by the batch.  For decode these are the EXPECTED
- * values the header must carry.  kv_block entries must lie in [0, pages in the KV pool). */
+ * values the header must carry.  kv_block entries must lie in [0, pages in the KV pool).
+ * options: ZTCP_OPT_* bits (0 = the reference's scalar x86-64 arithmetic, bit-exact with its build). */
+#define ZTCP_OPT_NEON_ARITH 1 /* egress: quantize with the reference's ARM NEON fp16 arithmetic (its build with
+                                 __ARM_FEATURE_FP16_VECTOR_ARITHMETIC, csrc:718-733 / :786-803); decode ignores it */
 typedef struct ztcp_page_batch {
   int64_t n_pages;
   const int32_t* kv_block;
@@ -81,7 +84,7 @@ typedef struct ztcp_page_batch {
   uint32_t model_id_hash;
   uint16_t layer_id_uniform;
   uint16_t head_group_id;
-  int32_t reserved;
+  int32_t options;
 } ztcp_page_batch;
 
 /* Message of the last failed call on this thread ("" when none). */

@@ -235,6 +235,64 @@ static void quant_group_int4(const uint16_t* src, uint8_t* q, uint16_t* scale) {
   }
 }
 
+/* ------------------------------------------------------------------ */
+/* Group-16 quantizers, ARM NEON semantics (the reference built with     */
+/* __ARM_FEATURE_FP16_VECTOR_ARITHMETIC: csrc:718-733 INT8, :786-803 INT4; */
+/* its dual- and quad-group paths :905-1039 take the same per-group      */
+/* steps).  |x| max in fp16 with NaN propagating (FMAX), the 1e-6 floor  */
+/* through std::max, scale = fp16(amax * (1/qmax)), inv = fp16(1/scale) */
+/* held in an fp16 register, the product x*inv rounded to fp16 (the     */
+/* product of two fp16 values is exact in float), then vcvtn (nearest,  */
+/* ties to even, NaN -> 0, saturating to int16) and vqmovn / vqmovun    */
+/* narrowing.  Dequantization is the same as the scalar path's: the      */
+/* fp16 product of q and the scale is rounded once either way.           */
+/* Not checked against an ARM build (none runs here).                    */
+/* ------------------------------------------------------------------ */
+static float neon_amax(const uint16_t* src) {
+  float m = fabsf(zo_f16_to_f32(src[0]));
+  for (int i = 1; i < ZO_GROUP; ++i) {
+    float a = fabsf(zo_f16_to_f32(src[i]));
+    m = (isnan(m) || isnan(a)) ? NAN : (a > m ? a : m);
+  }
+  return m < 1e-6f ? 1e-6f : m; /* std::max(amax, 1e-6f) keeps a NaN */
+}
+
+static int32_t neon_cvtn_s16(uint16_t h) {
+  float f = zo_f16_to_f32(h);
+  if (isnan(f)) return 0;
+  float r = nearbyintf(f);
+  if (r > 32767.0f) return 32767;
+  if (r < -32768.0f) return -32768;
+  return (int32_t)r;
+}
+
+static uint16_t neon_inv(uint16_t sh) { return zo_f32_to_f16(1.0f / zo_f16_to_f32(sh)); }
+
+static void quant_group_int8_neon(const uint16_t* src, uint8_t* q, uint16_t* scale) {
+  uint16_t sh = zo_f32_to_f16(neon_amax(src) * (1.0f / 127.0f));
+  float inv = zo_f16_to_f32(neon_inv(sh));
+  *scale = sh;
+  for (int i = 0; i < ZO_GROUP; ++i) {
+    int32_t s = neon_cvtn_s16(zo_f32_to_f16(zo_f16_to_f32(src[i]) * inv));
+    s = s > 127 ? 127 : (s < -128 ? -128 : s); /* vqmovn_s16 */
+    if (s < -127) s = -127;                     /* vmaxq_s8(q, -127) */
+    q[i] = (uint8_t)(int8_t)s;
+  }
+}
+
+static void quant_group_int4_neon(const uint16_t* src, uint8_t* q, uint16_t* scale) {
+  uint16_t sh = zo_f32_to_f16(neon_amax(src) * (1.0f / 7.0f));
+  float inv = zo_f16_to_f32(neon_inv(sh));
+  *scale = sh;
+  int u[ZO_GROUP];
+  for (int i = 0; i < ZO_GROUP; ++i) {
+    int16_t s = (int16_t)(neon_cvtn_s16(zo_f32_to_f16(zo_f16_to_f32(src[i]) * inv)) + 8); /* vaddq_s16 wraps */
+    int v = s < 0 ? 0 : (s > 255 ? 255 : s);                                                /* vqmovun_s16 */
+    u[i] = v > 15 ? 15 : v;                                                                 /* vminq_u8 */
+  }
+  for (int i = 0; i < ZO_GROUP / 2; ++i) q[i] = (uint8_t)(u[2 * i] | (u[2 * i + 1] << 4));
+}
+
 static void dequant_group_int8(const uint8_t* q, uint16_t scale, uint16_t* dst) {
   float s = zo_f16_to_f32(scale);
   for (int i = 0; i < ZO_GROUP; ++i) dst[i] = zo_f32_to_f16((float)(int8_t)q[i] * s);
@@ -305,10 +363,10 @@ static void write_header(uint8_t* h, int preset, int rope_mode, uint32_t tenant,
  * (v may be NULL for a single-buffer MLA page).  blob_out must hold
  * 32 + expected_payload + 16 bytes.  Returns 0, or -1 on invalid arguments.
  */
-int zo_encode_page(const uint16_t* k, const uint16_t* v, int64_t vecs, int64_t head_dim, int64_t rope_dim,
-                   int preset, int rope_mode, int64_t expected_payload, uint32_t tenant, uint32_t model,
-                   uint16_t layer, uint16_t head_group, uint64_t tok, uint64_t seq, const uint64_t key[4],
-                   uint64_t mk0, uint64_t mk1, uint8_t* blob_out) {
+static int encode_page(const uint16_t* k, const uint16_t* v, int64_t vecs, int64_t head_dim, int64_t rope_dim,
+                       int preset, int rope_mode, int64_t expected_payload, uint32_t tenant, uint32_t model,
+                       uint16_t layer, uint16_t head_group, uint64_t tok, uint64_t seq, const uint64_t key[4],
+                       uint64_t mk0, uint64_t mk1, uint8_t* blob_out, int neon) {
   int64_t min_p = zo_min_payload_bytes(preset, rope_mode, vecs, head_dim, rope_dim, v != NULL);
   if (min_p < 0 || expected_payload < min_p) return -1;
   uint8_t* hdr = blob_out;
@@ -339,8 +397,9 @@ int zo_encode_page(const uint16_t* k, const uint16_t* v, int64_t vecs, int64_t h
       for (int64_t g = 0; g < groups; ++g) {
         const uint16_t* src = buf + r * head_dim + sec[si].col + g * ZO_GROUP;
         uint16_t sc;
-        if (sec[si].kind == 1) quant_group_int8(src, qbase + (r * groups + g) * qpg, &sc);
-        else quant_group_int4(src, qbase + (r * groups + g) * qpg, &sc);
+        uint8_t* qd = qbase + (r * groups + g) * qpg;
+        if (sec[si].kind == 1) (neon ? quant_group_int8_neon : quant_group_int8)(src, qd, &sc);
+        else (neon ? quant_group_int4_neon : quant_group_int4)(src, qd, &sc);
         sbase[2 * (r * groups + g)] = (uint8_t)sc;
         sbase[2 * (r * groups + g) + 1] = (uint8_t)(sc >> 8);
       }
@@ -354,6 +413,14 @@ int zo_encode_page(const uint16_t* k, const uint16_t* v, int64_t vecs, int64_t h
   zo_siphash128(mk0, mk1, blob_out, (size_t)(ZO_HEADER_BYTES + expected_payload),
                 blob_out + ZO_HEADER_BYTES + expected_payload);
   return 0;
+}
+
+int zo_encode_page(const uint16_t* k, const uint16_t* v, int64_t vecs, int64_t head_dim, int64_t rope_dim,
+                   int preset, int rope_mode, int64_t expected_payload, uint32_t tenant, uint32_t model,
+                   uint16_t layer, uint16_t head_group, uint64_t tok, uint64_t seq, const uint64_t key[4],
+                   uint64_t mk0, uint64_t mk1, uint8_t* blob_out) {
+  return encode_page(k, v, vecs, head_dim, rope_dim, preset, rope_mode, expected_payload, tenant, model, layer,
+                     head_group, tok, seq, key, mk0, mk1, blob_out, 0);
 }
 
 /*
@@ -434,18 +501,28 @@ int zo_decode_page(const uint8_t* blob, int64_t blob_len, int64_t vecs, int64_t 
  * Decode returns the index of the first failing page, or -1 when all pass;
  * per-page statuses go to status_out.
  */
+/* arith: 0 = the reference's scalar (x86-64) quantizers, 1 = its ARM NEON fp16 quantizers */
+int zo_encode_batch_arith(const uint16_t* k, const uint16_t* v, int64_t batch, int64_t vecs, int64_t head_dim,
+                          int64_t rope_dim, int preset, int rope_mode, int64_t expected_payload, uint32_t tenant,
+                          uint32_t model, uint16_t layer, uint16_t head_group, const uint64_t* tok,
+                          uint64_t base_seq, const uint64_t key[4], uint64_t mk0, uint64_t mk1, uint8_t* blobs_out,
+                          int arith) {
+  int64_t page = vecs * head_dim, blob = ZO_HEADER_BYTES + expected_payload + ZO_TAG_BYTES;
+  for (int64_t b = 0; b < batch; ++b) {
+    int rc = encode_page(k + b * page, v ? v + b * page : NULL, vecs, head_dim, rope_dim, preset, rope_mode,
+                         expected_payload, tenant, model, layer, head_group, tok[b], base_seq + (uint64_t)b, key,
+                         mk0, mk1, blobs_out + b * blob, arith);
+    if (rc) return rc;
+  }
+  return 0;
+}
+
 int zo_encode_batch(const uint16_t* k, const uint16_t* v, int64_t batch, int64_t vecs, int64_t head_dim,
                     int64_t rope_dim, int preset, int rope_mode, int64_t expected_payload, uint32_t tenant,
                     uint32_t model, uint16_t layer, uint16_t head_group, const uint64_t* tok, uint64_t base_seq,
                     const uint64_t key[4], uint64_t mk0, uint64_t mk1, uint8_t* blobs_out) {
-  int64_t page = vecs * head_dim, blob = ZO_HEADER_BYTES + expected_payload + ZO_TAG_BYTES;
-  for (int64_t b = 0; b < batch; ++b) {
-    int rc = zo_encode_page(k + b * page, v ? v + b * page : NULL, vecs, head_dim, rope_dim, preset, rope_mode,
-                            expected_payload, tenant, model, layer, head_group, tok[b], base_seq + (uint64_t)b,
-                            key, mk0, mk1, blobs_out + b * blob);
-    if (rc) return rc;
-  }
-  return 0;
+  return zo_encode_batch_arith(k, v, batch, vecs, head_dim, rope_dim, preset, rope_mode, expected_payload, tenant,
+                               model, layer, head_group, tok, base_seq, key, mk0, mk1, blobs_out, 0);
 }
 
 int64_t zo_decode_batch(const uint8_t* blobs, int64_t batch, int64_t blob_len, int64_t vecs, int64_t head_dim,

@@ -61,6 +61,8 @@ def lib():
         L.zo_encode_batch.argtypes = [u16p, u16p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int, C.c_int,
                                       C.c_int64, C.c_uint32, C.c_uint32, C.c_uint16, C.c_uint16, u64p, C.c_uint64,
                                       u64p, C.c_uint64, C.c_uint64, u8p]
+        L.zo_encode_batch_arith.restype = C.c_int
+        L.zo_encode_batch_arith.argtypes = L.zo_encode_batch.argtypes + [C.c_int]
         L.zo_decode_batch.restype = C.c_int64
         L.zo_decode_batch.argtypes = [u8p, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int64, C.c_int,
                                       C.c_uint32, C.c_uint32, C.c_uint16, u64p, u64p, C.c_uint64, C.c_uint64,
@@ -118,10 +120,12 @@ def spec_payload_bytes(preset, rope_mode, vecs, head_dim, rope_dim, has_v) -> in
 
 
 def encode_batch(k_f16: np.ndarray, v_f16: np.ndarray | None, token_hashes, *, rope_dim, preset, rope_mode,
-                 expected_payload, tenant, model, layer, head_group, base_seq, key, mac_key) -> np.ndarray:
+                 expected_payload, tenant, model, layer, head_group, base_seq, key, mac_key,
+                 neon: bool = False) -> np.ndarray:
     """Reference batch-egress semantics (page b gets sequence_nonce = base_seq + b).
 
     k_f16/v_f16: uint16 [batch, tokens, heads, head_dim] (fp16 bits).  Returns uint8 [batch, blob_bytes].
+    neon: quantize with the reference's ARM NEON fp16 arithmetic instead of its scalar x86 path.
     """
     k = np.ascontiguousarray(k_f16, np.uint16)
     v = None if v_f16 is None else np.ascontiguousarray(v_f16, np.uint16)
@@ -130,11 +134,11 @@ def encode_batch(k_f16: np.ndarray, v_f16: np.ndarray | None, token_hashes, *, r
     tok = np.ascontiguousarray(np.asarray(token_hashes, dtype=np.uint64))
     keyarr = np.asarray([int(x) & (2**64 - 1) for x in key], np.uint64)
     out = np.zeros((b, HEADER_BYTES + expected_payload + TAG_BYTES), np.uint8)
-    rc = lib().zo_encode_batch(_p(k, C.c_uint16), None if v is None else _p(v, C.c_uint16), b, vecs, d, rope_dim,
-                               int(preset), int(rope_mode), expected_payload, tenant & 0xFFFFFFFF,
-                               model & 0xFFFFFFFF, layer & 0xFFFF, head_group & 0xFFFF, _p(tok, C.c_uint64),
-                               base_seq & (2**64 - 1), _p(keyarr, C.c_uint64), int(mac_key[0]) & (2**64 - 1),
-                               int(mac_key[1]) & (2**64 - 1), _p(out, C.c_uint8))
+    rc = lib().zo_encode_batch_arith(_p(k, C.c_uint16), None if v is None else _p(v, C.c_uint16), b, vecs, d,
+                                     rope_dim, int(preset), int(rope_mode), expected_payload, tenant & 0xFFFFFFFF,
+                                     model & 0xFFFFFFFF, layer & 0xFFFF, head_group & 0xFFFF, _p(tok, C.c_uint64),
+                                     base_seq & (2**64 - 1), _p(keyarr, C.c_uint64), int(mac_key[0]) & (2**64 - 1),
+                                     int(mac_key[1]) & (2**64 - 1), _p(out, C.c_uint8), int(bool(neon)))
     if rc != 0:
         raise ValueError("oracle encode rejected its arguments")
     return out

@@ -425,3 +425,53 @@ def test_bf16_groups_at_the_fp16_boundary(ext, oracle, preset, rope_mode):
     blobs = gpu_encode(ext, kb, vb, torch.from_numpy(toks), 16, preset, rope_mode, exp, m)
     want = helpers.oracle_encode(oracle, kb.half().numpy(), vb.half().numpy(), toks, 16, preset, rope_mode, exp, m)
     np.testing.assert_array_equal(blobs.cpu().numpy(), want)
+
+
+@pytest.mark.parametrize("mla", [False, True])
+def test_neon_arithmetic_option(ext, oracle, mla):
+    """The batch option that quantizes with the reference's ARM NEON fp16 arithmetic: bytes equal the
+    oracle's NEON restatement (itself cross-checked against a numpy restatement; no ARM build runs
+    here), on every preset x RoPE mode with edge values, fp16 and bf16 input; the standard ingress decodes
+    the blobs (dequantization is the same in both arithmetics)."""
+    from ztcp_b200 import capi, codec, workload
+
+    rng = np.random.default_rng(17 + mla)
+    T, H, D, rope = (16, 1, 96, 32) if mla else (16, 2, 64, 16)
+    edge = np.array([np.inf, -np.inf, 65504, -65504, 1e-7, -3e-6, 0.0, 7e4], dtype=np.float32)
+    for preset in (1, 2, 3):
+        for rope_mode in (0, 1, 2):
+            for bf16 in (False, True):
+                x = (rng.standard_normal((2, 3, T, H, D)) * 10.0 ** rng.uniform(-4, 3)).astype(np.float32)
+                mask = rng.random(x.shape) < 0.02
+                x[mask] = rng.choice(edge, int(mask.sum()))
+                if bf16:
+                    kt = torch.from_numpy(x[0]).to(torch.bfloat16)
+                    vt = None if mla else torch.from_numpy(x[1]).to(torch.bfloat16)
+                    k16 = kt.half().numpy()
+                    v16 = None if mla else vt.half().numpy()
+                else:
+                    with np.errstate(over="ignore"):  # 7e4 overflows to inf on purpose
+                        k16 = x[0].astype(np.float16)
+                        v16 = None if mla else x[1].astype(np.float16)
+                    kt, vt = torch.from_numpy(k16), None if mla else torch.from_numpy(v16)
+                m = workload.session_material(int(rng.integers(1 << 30)))
+                toks = workload.token_hashes(3, int(rng.integers(1 << 30)))
+                exp = oracle.spec_payload_bytes(preset, rope_mode, T * H, D, rope, not mla)
+                keys = capi.keys(*m["key"], *m["mac_key"])
+                blobs = torch.empty((3, 48 + exp), dtype=torch.uint8, device=DEV)
+                codec.encode_pages(kt.to(DEV), None if vt is None else vt.to(DEV), torch.from_numpy(toks).to(DEV),
+                                   blobs, rope_dim=rope, preset=preset, rope_mode=rope_mode,
+                                   expected_payload_bytes=exp, tenant_id_hash=m["tenant"], model_id_hash=m["model"],
+                                   layer_id=m["layer"], head_group_id=m["head_group"],
+                                   base_sequence_nonce=m["base_seq"], keys=keys, neon_arith=True)
+                want = oracle.encode_batch(k16.view(np.uint16), None if v16 is None else v16.view(np.uint16), toks,
+                                           rope_dim=rope, preset=preset, rope_mode=rope_mode, expected_payload=exp,
+                                           tenant=m["tenant"], model=m["model"], layer=m["layer"],
+                                           head_group=m["head_group"], base_seq=m["base_seq"], key=m["key"],
+                                           mac_key=m["mac_key"], neon=True)
+                tag = f"preset{preset} mode{rope_mode} mla{mla} bf16{bf16}"
+                np.testing.assert_array_equal(blobs.cpu().numpy(), want, err_msg=tag)
+                kd, vd = gpu_decode(ext, blobs, torch.from_numpy(toks), k16.shape, rope, mla, m)
+                okd, ovd, _, first = helpers.oracle_decode(oracle, want, toks, k16.shape, rope, mla, m)
+                assert first == -1
+                np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd, err_msg=tag)

@@ -145,3 +145,53 @@ def test_oracle_matches_reference_build(oracle, preset, rope_mode, mla):
             m["key"][1], m["mac_key"][0], m["mac_key"][1], m["key"][2], m["key"][3])
         mine = helpers.oracle_encode(oracle, k, v, toks, rope, preset, rope_mode, exp, m)
         np.testing.assert_array_equal(mine, out.numpy())
+
+
+def _neon_group(x16: np.ndarray, qmax: int):
+    """Independent numpy restatement of the reference's ARM NEON group quantizer (fp16 arithmetic)."""
+    a = np.abs(x16.astype(np.float32))
+    m = a[0]
+    for val in a[1:]:
+        m = np.float32(np.nan) if (np.isnan(m) or np.isnan(val)) else max(m, val)
+    amax = np.float32(1e-6) if m < np.float32(1e-6) else m
+    sh = np.float16(np.float32(amax) * (np.float32(1.0) / np.float32(qmax)))
+    with np.errstate(all="ignore"):
+        inv = np.float16(np.float32(1.0) / np.float32(sh))
+        p = (x16.astype(np.float32) * np.float32(inv)).astype(np.float16).astype(np.float32)
+    s = np.where(np.isnan(p), 0, np.clip(np.rint(np.nan_to_num(p, nan=0.0)), -32768, 32767)).astype(np.int32)
+    if qmax == 127:
+        q = np.maximum(np.clip(s, -128, 127), -127).astype(np.int8).view(np.uint8)
+        return q, sh
+    u = np.minimum(np.clip((s + 8).astype(np.int16).astype(np.int32), 0, 255), 15)
+    return (u[0::2] | (u[1::2] << 4)).astype(np.uint8), sh
+
+
+@pytest.mark.parametrize("preset", [1, 3])
+def test_neon_mode_matches_numpy_restatement(oracle, preset):
+    from ztcp_b200 import workload
+
+    rng = np.random.default_rng(preset)
+    edge = np.array([np.inf, -np.inf, np.nan, 65504, -65504, 7e4, 1e-7, -6e-8, 0.0, 3.0e-5], dtype=np.float32)
+    m = workload.session_material(9)
+    qmax = 7 if preset == 1 else 127
+    qb = 8 if preset == 1 else 16
+    for trial in range(300):
+        scale_mag = 10.0 ** rng.uniform(-9, 5)
+        x = (rng.standard_normal((2, 16)) * scale_mag).astype(np.float32)
+        if trial % 3 == 0:
+            x.flat[rng.integers(0, 32, 3)] = rng.choice(edge, 3)
+        x16 = x.astype(np.float16)
+        k = x16[0].reshape(1, 1, 1, 16)
+        v = x16[1].reshape(1, 1, 1, 16)
+        exp = oracle.spec_payload_bytes(preset, 0, 1, 16, 0, True)
+        blob = oracle.encode_batch(k.view(np.uint16), v.view(np.uint16), np.array([5], np.uint64), rope_dim=0,
+                                   preset=preset, rope_mode=0, expected_payload=exp, tenant=1, model=2, layer=3,
+                                   head_group=4, base_seq=trial, key=m["key"], mac_key=m["mac_key"], neon=True)[0]
+        key32 = b"".join(int(w).to_bytes(8, "little") for w in m["key"])
+        nonce = struct.pack("<3I", trial & 0xFFFFFFFF, trial >> 32, (3 << 16) | 4)
+        pt = np.frombuffer(oracle.chacha20_xor(bytes(blob[32:32 + exp]), key32, 1, nonce), np.uint8)
+        for part in range(2):  # K then V: [q][scale]
+            off = part * (qb + 2)
+            q_ref, sh_ref = _neon_group(x16[part], qmax)
+            np.testing.assert_array_equal(pt[off:off + qb], q_ref, err_msg=f"trial {trial} part {part}")
+            assert pt[off + qb:off + qb + 2].view(np.uint16)[0] == sh_ref.view(np.uint16), (trial, part)

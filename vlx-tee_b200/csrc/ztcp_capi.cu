@@ -44,6 +44,7 @@ int32_t check_batch(const ztcp_page_batch* b) {
   if (!b) return fail(ZTCP_EINVAL, "page batch must not be NULL");
   if (b->n_pages <= 0) return fail(ZTCP_EINVAL, "batch must hold at least one page");
   if (!b->token_hash) return fail(ZTCP_EINVAL, "page_token_hashes must not be NULL");
+  if (b->options & ~ZTCP_OPT_NEON_ARITH) return fail(ZTCP_EINVAL, "unknown page batch options");
   return ZTCP_OK;
 }
 
@@ -137,6 +138,7 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
   P.head_dim = (int32_t)geom->head_dim;
   P.flags = (preset & 0x0F) | ((rope_mode & 0x0F) << 4);
   P.meta = to_meta(batch);
+  P.neon_arith = (batch->options & ZTCP_OPT_NEON_ARITH) != 0;
   key_words(keys, P.key);
   P.tile_vecs = pick_tile_vecs(vecs, ztcp::stage_bytes_per_vec(P.L));
   P.n_tiles = (int32_t)((vecs + P.tile_vecs - 1) / P.tile_vecs);

@@ -355,6 +355,64 @@ __device__ __forceinline__ bool quant_int8_bf16(const uint32_t w[8], uint32_t q[
 }
 
 // ------------------------------------------------------------------------------------------------
+// Group-16 quantizers with the reference's ARM NEON fp16 arithmetic (csrc:718-733 INT8, :786-803 INT4;
+// the multi-group NEON paths :905-1039 take the same per-group steps): |x| max in fp16 with NaN
+// propagating, the 1e-6 floor through std::max, scale = fp16(amax * (1/qmax)), inv = fp16(1/scale),
+// each product x*inv rounded to fp16 (the product of two fp16 values is exact in fp32), then
+// round-to-nearest-even to int16 (NaN -> 0, saturating) and the saturating narrowings of vqmovn /
+// vqmovun.  Selected per call; dequantization is the same in both arithmetics.
+// ------------------------------------------------------------------------------------------------
+__device__ __forceinline__ float neon_amax(const uint32_t w[8]) {
+  float m = fabsf(f16_at(w, 0));
+#pragma unroll
+  for (int i = 1; i < 16; ++i) {
+    const float a = fabsf(f16_at(w, i));
+    m = (m != m || a != a) ? __int_as_float(0x7FC00000) : (a > m ? a : m);
+  }
+  return m < 1e-6f ? 1e-6f : m;
+}
+
+__device__ __forceinline__ int32_t neon_cvtn_s16(float p) {
+  if (p != p) return 0;
+  return (int32_t)fminf(fmaxf(rintf(p), -32768.0f), 32767.0f);
+}
+
+// fp16(x * inv) for fp16 x and inv, as an fp32 value
+__device__ __forceinline__ float neon_mul(float x, float inv) { return __half2float(__float2half_rn(__fmul_rn(x, inv))); }
+
+__device__ __forceinline__ uint16_t quant_int8_neon(const uint32_t w[8], uint32_t q[4]) {
+  const __half sh = __float2half_rn(__fmul_rn(neon_amax(w), 1.0f / 127.0f));
+  const float inv = __half2float(__float2half_rn(__frcp_rn(__half2float(sh))));
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int32_t s = max(min(neon_cvtn_s16(neon_mul(f16_at(w, 4 * k + j), inv)), 127), -127);
+      word |= ((uint32_t)s & 0xFFu) << (8 * j);
+    }
+    q[k] = word;
+  }
+  return __half_as_ushort(sh);
+}
+
+__device__ __forceinline__ uint16_t quant_int4_neon(const uint32_t w[8], uint32_t q[2]) {
+  const __half sh = __float2half_rn(__fmul_rn(neon_amax(w), 1.0f / 7.0f));
+  const float inv = __half2float(__float2half_rn(__frcp_rn(__half2float(sh))));
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    uint32_t word = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int32_t s = (int16_t)(neon_cvtn_s16(neon_mul(f16_at(w, 8 * k + j), inv)) + 8);  // int16 add wraps
+      word |= (uint32_t)min(max(s, 0), 15) << (4 * j);
+    }
+    q[k] = word;
+  }
+  return __half_as_ushort(sh);
+}
+
+// ------------------------------------------------------------------------------------------------
 // Dequantizers: fp16(float(q) * float(scale)).  float(q) * float(scale) is exact in fp32 (<= 8 + 11
 // significant bits), so one IEEE half multiply of half(q) by the scale rounds it identically; half(q)
 // is built exactly as (1024 + u) - bias from the bit pattern 0x6400 | u.  A non-finite scale takes the

@@ -124,7 +124,7 @@ __device__ __forceinline__ void split_item(int it, const SectionTile& t, int& ve
   }
 }
 
-template <int KIND, bool BF16>
+template <int KIND, bool BF16, bool NEON>
 __device__ __forceinline__ void quantize_section(const SectionTile& t) {
   const int items = t.tv * t.groups;
   for (int it = threadIdx.x; it < items; it += blockDim.x) {
@@ -144,24 +144,24 @@ __device__ __forceinline__ void quantize_section(const SectionTile& t) {
     } else if (KIND == kInt8) {
       uint32_t q[4];
       uint16_t sc;
-      if (!BF16 || !quant_int8_bf16(w, q, &sc)) {
+      if (NEON || !BF16 || !quant_int8_bf16(w, q, &sc)) {
         if (BF16) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
         }
-        sc = quant_int8(w, q);
+        sc = NEON ? quant_int8_neon(w, q) : quant_int8(w, q);
       }
       *reinterpret_cast<uint4*>(qd + g * 16) = make_uint4(q[0], q[1], q[2], q[3]);
       *reinterpret_cast<uint16_t*>(t.sc + vec * t.s_bpv + g * 2) = sc;
     } else {
       uint32_t q[2];
       uint16_t sc;
-      if (!BF16 || !quant_int4_bf16(w, q, &sc)) {
+      if (NEON || !BF16 || !quant_int4_bf16(w, q, &sc)) {
         if (BF16) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
         }
-        sc = quant_int4(w, q);
+        sc = NEON ? quant_int4_neon(w, q) : quant_int4(w, q);
       }
       *reinterpret_cast<uint2*>(qd + g * 8) = make_uint2(q[0], q[1]);
       *reinterpret_cast<uint16_t*>(t.sc + vec * t.s_bpv + g * 2) = sc;
@@ -208,7 +208,7 @@ __device__ __forceinline__ int32_t log2_if_pow2(int32_t x) {
 // Egress: quantize + pack + encrypt one (page, vec-tile)
 // ------------------------------------------------------------------------------------------------
 // 7 resident CTAs per SM (the register cap this implies was measured ~5 % faster than 6).
-template <bool BF16>
+template <bool BF16, bool NEON>
 __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __grid_constant__ EgressParams P) {
   extern __shared__ __align__(16) uint8_t stage[];
   __shared__ RangeTable T;
@@ -229,9 +229,9 @@ __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __gr
     const Section S = P.L.sec[s];
     const SectionTile st{(S.buf ? vp : kp) + v0 * P.head_dim + S.col, stage + P.stage_q[s], stage + P.stage_s[s],
                          P.head_dim, S.q_bpv, S.s_bpv, S.dim >> 4, P.gshift[s], tv};
-    if (S.kind == kInt4) quantize_section<kInt4, BF16>(st);
-    else if (S.kind == kInt8) quantize_section<kInt8, BF16>(st);
-    else quantize_section<kRaw, BF16>(st);
+    if (S.kind == kInt4) quantize_section<kInt4, BF16, NEON>(st);
+    else if (S.kind == kInt8) quantize_section<kInt8, BF16, NEON>(st);
+    else quantize_section<kRaw, BF16, NEON>(st);
   }
 
   // header (32 bytes) by tile 0
@@ -592,14 +592,20 @@ void ensure_smem(K kernel, int32_t bytes) {
 
 }  // namespace
 
-void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream) {
+template <bool BF16, bool NEON>
+void launch_egress_t(const EgressParams& P, cudaStream_t stream) {
   const int64_t grid = P.n_pages * P.n_tiles;
-  if (bf16) {
-    ensure_smem(egress_tile_kernel<true>, P.stage_bytes);
-    egress_tile_kernel<true><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+  ensure_smem(egress_tile_kernel<BF16, NEON>, P.stage_bytes);
+  egress_tile_kernel<BF16, NEON><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+}
+
+void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream) {
+  if (P.neon_arith) {
+    if (bf16) launch_egress_t<true, true>(P, stream);
+    else launch_egress_t<false, true>(P, stream);
   } else {
-    ensure_smem(egress_tile_kernel<false>, P.stage_bytes);
-    egress_tile_kernel<false><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+    if (bf16) launch_egress_t<true, false>(P, stream);
+    else launch_egress_t<false, false>(P, stream);
   }
 }
 

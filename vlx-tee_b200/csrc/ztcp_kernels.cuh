@@ -42,6 +42,7 @@ struct EgressParams {
   int32_t stage_s[3];
   int32_t gshift[3];        // log2(groups per row) of each section, -1 when not a power of two
   int32_t stage_bytes;
+  int32_t neon_arith;       // quantize with the reference's ARM NEON fp16 arithmetic
 };
 
 struct MacParams {

@@ -65,8 +65,11 @@ class PageBatch(C.Structure):
         ("model_id_hash", C.c_uint32),
         ("layer_id_uniform", C.c_uint16),
         ("head_group_id", C.c_uint16),
-        ("reserved", C.c_int32),
+        ("options", C.c_int32),
     ]
+
+
+OPT_NEON_ARITH = 1
 
 
 class ZtcpError(RuntimeError):

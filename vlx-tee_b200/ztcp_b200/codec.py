@@ -82,10 +82,12 @@ def encode_pages(k_pool: torch.Tensor, v_pool: torch.Tensor | None, token_hashes
                  tenant_id_hash: int, model_id_hash: int, layer_id: int, head_group_id: int,
                  base_sequence_nonce: int, keys: capi.Keys, block_table: torch.Tensor | None = None,
                  sequence_nonces: torch.Tensor | None = None, layer_ids: torch.Tensor | None = None,
-                 check_block_table: bool = True) -> None:
+                 check_block_table: bool = True, neon_arith: bool = False) -> None:
     """Egress of ``out_blobs.shape[0]`` pages from a KV pool [pool_pages, T, H, D] (fp16 or bf16).
 
-    Page i reads pool block ``block_table[i]`` (default i) and is written to out_blobs[i].
+    Page i reads pool block ``block_table[i]`` (default i) and is written to out_blobs[i].  With
+    ``neon_arith`` the groups are quantized with the reference's ARM NEON fp16 arithmetic (the bytes its
+    ARM build writes) instead of its scalar x86-64 arithmetic.
     """
     dev = k_pool.device
     _require_cuda("k_pages", k_pool, (torch.float16, torch.bfloat16))
@@ -110,6 +112,7 @@ def encode_pages(k_pool: torch.Tensor, v_pool: torch.Tensor | None, token_hashes
     geom = capi.geometry(T, H, D, rope_dim, v_pool is None)
     batch = _page_batch(n, token_hashes, block_table, sequence_nonces, layer_ids, base_sequence_nonce,
                         tenant_id_hash, model_id_hash, layer_id, head_group_id)
+    batch.options = capi.OPT_NEON_ARITH if neon_arith else 0
     dtype = capi.DTYPE_BF16 if k_pool.dtype == torch.bfloat16 else capi.DTYPE_F16
     lib = capi.load()
     with torch.cuda.device(dev):
