@@ -139,6 +139,7 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
   P.flags = (preset & 0x0F) | ((rope_mode & 0x0F) << 4);
   P.meta = to_meta(batch);
   P.neon_arith = (batch->options & ZTCP_OPT_NEON_ARITH) != 0;
+  P.mul = ztcp::PackMul{16u, 256u, 65536u};
   key_words(keys, P.key);
   P.tile_vecs = pick_tile_vecs(vecs, ztcp::stage_bytes_per_vec(P.L));
   P.n_tiles = (int32_t)((vecs + P.tile_vecs - 1) / P.tile_vecs);

@@ -13,6 +13,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include "ztcp_layout.h"
+
 namespace ztcp {
 
 // ------------------------------------------------------------------------------------------------
@@ -235,20 +237,55 @@ __device__ __forceinline__ void quant_int4_exact(const uint32_t* w, float inv, u
 // ------------------------------------------------------------------------------------------------
 // Group-16 quantizers.  scale = fp16(amax / qmax) and inv = 1 / float(scale) (IEEE reciprocal).
 // Fast path: every element finite and scale a normal fp16.  Then the scale is within 2^-11 of
-// amax / qmax, so |x * inv| <= qmax * (1 + 2^-11) + tiny < qmax + 0.5 and no clamp can fire; rint is
-// the FADD of 1.5 * 2^23 (round-to-nearest-even at integer granularity, exact for |p| < 2^22) whose
-// low bits are rint(p) in two's complement.  fp16(amax / qmax) equals fp16(amax * (1 / qmax)) for
-// every fp16 amax and the 1e-6 floor (checked exhaustively by the CPU tests), so the scale is one
-// multiply.
+// amax / qmax, so |x * inv| <= qmax * (1 + 2^-11) + tiny < qmax + 0.5 and no clamp can fire.  fp16(amax /
+// qmax) equals fp16(amax * (1 / qmax)) for every fp16 amax and the 1e-6 floor (checked exhaustively by the
+// CPU tests), so the scale is one multiply.
+//
+// Rounding and packing.  p = x * inv rounded to fp32, then p + M with M = 2^23 + c rounded again: the sum
+// lies in [2^23, 2^24), where the fp32 spacing is 1, so the FADD rounds p to the nearest integer with ties
+// to even (M is even) and the sum's bit pattern is 0x4B000000 + (M - 2^23) + rint(p).  With c = qmax + 1
+// (8 for INT4, 128 for INT8) the low bits hold u = rint(p) + c, in [1, 15] or [1, 255].  The stored word is
+// then the sum of the element patterns weighted 16^i (INT4 nibble i) or 256^i (INT8 byte i), mod 2^32:
+// the u terms land in their own nibbles or bytes without carries, and the constant parts cancel because
+// one element's magic carries an extra offset (0x500000 at nibble 1, 0xB500 at byte 2) chosen so that
+// the sum of all constant terms is 2^32.  So each element costs one multiply, one add and one integer
+// multiply-add.  INT4 stores u itself (the format's q + 8); INT8 stores q = u - 128 as a two's-complement
+// byte, which is u with its top bit flipped (one XOR per word).  The multiply and the add are the scalar
+// _rn intrinsics, never contracted into a fused multiply-add: a fused x * inv + M would break rounding
+// ties with the unrounded product.  (Packed f32x2 multiply and add were observed to be fused on sm_100a
+// even with explicit .rn, so they are not used.)  The integer weights come from the kernel parameters
+// (PackMul) rather than literals: with a literal power of two the compiler turns each multiply-add into a
+// shift-and-add on the integer ALU pipe, which ChaCha20 already saturates; as IMADs they run on the FMA pipe.
 // ------------------------------------------------------------------------------------------------
-constexpr float kRoundMagic = 12582912.0f;  // 1.5 * 2^23
+constexpr float kPackM4 = 8388616.0f;             // 2^23 + 8
+constexpr float kPackM4n1 = 8388616.0f + 5242880.0f;  // 2^23 + 8 + 0x500000 (nibble 1)
+constexpr float kPackM8 = 8388736.0f;             // 2^23 + 128
+constexpr float kPackM8b2 = 8388736.0f + 46336.0f;    // 2^23 + 128 + 0xB500 (byte 2)
 
-// x * inv rounded to fp32, then + 1.5 * 2^23 rounded again.  Both steps are the scalar _rn intrinsics,
-// which are never contracted into a fused multiply-add: a fused x * inv + 1.5 * 2^23 would break
-// rounding ties (p = k + 0.5 after the fp32 multiply) with the unrounded product.  (Packed f32x2
-// multiply and add were observed to be fused on sm_100a even with explicit .rn, so they are not used.)
-__device__ __forceinline__ uint32_t round_bits(float x, float inv) {
-  return __float_as_uint(__fadd_rn(__fmul_rn(x, inv), kRoundMagic));
+__device__ __forceinline__ uint32_t pack_bits(float x, float inv, float m) {
+  return __float_as_uint(__fadd_rn(__fmul_rn(x, inv), m));
+}
+
+// Element pairs (lo = element 2j, hi = element 2j + 1) of one output word: INT4 eight elements from four
+// pairs, INT8 four elements from two pairs.
+__device__ __forceinline__ uint32_t pack_int4_word(const float lo[4], const float hi[4], float inv, const PackMul& mu) {
+  uint32_t acc = pack_bits(hi[3], inv, kPackM4);
+  acc = acc * mu.m16 + pack_bits(lo[3], inv, kPackM4);
+#pragma unroll
+  for (int j = 2; j >= 0; --j) {
+    acc = acc * mu.m16 + pack_bits(hi[j], inv, j == 0 ? kPackM4n1 : kPackM4);
+    acc = acc * mu.m16 + pack_bits(lo[j], inv, kPackM4);
+  }
+  return acc;
+}
+
+__device__ __forceinline__ uint32_t pack_int8_word(float e0, float e1, float e2, float e3, float inv,
+                                                   const PackMul& mu) {
+  uint32_t acc = pack_bits(e3, inv, kPackM8);
+  acc = acc * mu.m256 + pack_bits(e2, inv, kPackM8b2);
+  acc = acc * mu.m256 + pack_bits(e1, inv, kPackM8);
+  acc = acc * mu.m256 + pack_bits(e0, inv, kPackM8);
+  return acc ^ 0x80808080u;
 }
 
 __device__ __forceinline__ bool group_scale(const uint32_t w[8], float rq, __half* sh, float* inv) {
@@ -264,7 +301,7 @@ __device__ __forceinline__ bool group_scale(const uint32_t w[8], float rq, __hal
   return __half_as_ushort(*sh) >= 0x0400u;  // normal scale (finite: amax <= 65504)
 }
 
-__device__ __forceinline__ uint16_t quant_int8(const uint32_t w[8], uint32_t q[4]) {
+__device__ __forceinline__ uint16_t quant_int8(const uint32_t w[8], uint32_t q[4], const PackMul& mu) {
   __half sh;
   float inv;
   if (!group_scale(w, 1.0f / 127.0f, &sh, &inv)) {
@@ -275,14 +312,12 @@ __device__ __forceinline__ uint16_t quant_int8(const uint32_t w[8], uint32_t q[4
   for (int k = 0; k < 4; ++k) {
     const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * k]));
     const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&w[2 * k + 1]));
-    const uint32_t ab = __byte_perm(round_bits(a.x, inv), round_bits(a.y, inv), 0x0040);
-    const uint32_t cd = __byte_perm(round_bits(b.x, inv), round_bits(b.y, inv), 0x0040);
-    q[k] = __byte_perm(ab, cd, 0x5410);
+    q[k] = pack_int8_word(a.x, a.y, b.x, b.y, inv, mu);
   }
   return __half_as_ushort(sh);
 }
 
-__device__ __forceinline__ uint16_t quant_int4(const uint32_t w[8], uint32_t q[2]) {
+__device__ __forceinline__ uint16_t quant_int4(const uint32_t w[8], uint32_t q[2], const PackMul& mu) {
   __half sh;
   float inv;
   if (!group_scale(w, 1.0f / 7.0f, &sh, &inv)) {
@@ -291,16 +326,14 @@ __device__ __forceinline__ uint16_t quant_int4(const uint32_t w[8], uint32_t q[2
   }
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
-    uint32_t b[4];
+    float lo[4], hi[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const float2 x = __half22float2(*reinterpret_cast<const __half2*>(&w[4 * k + j]));
-      // low byte = nibble(e0) | nibble(e1) << 4, nibble = rint(p) mod 16 (the +8 comes below)
-      const uint32_t lo = round_bits(x.x, inv), hi = round_bits(x.y, inv) << 4;
-      b[j] = (lo & 0x0Fu) | (hi & 0xF0u);
+      lo[j] = x.x;
+      hi[j] = x.y;
     }
-    // bytes 0..3 of the word; +8 on all eight nibbles at once (flip bit 3: q + 8 in 4-bit two's complement)
-    q[k] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410) ^ 0x88888888u;
+    q[k] = pack_int4_word(lo, hi, inv, mu);
   }
   return __half_as_ushort(sh);
 }
@@ -314,31 +347,31 @@ __device__ __forceinline__ uint16_t quant_int4(const uint32_t w[8], uint32_t q[2
 // ------------------------------------------------------------------------------------------------
 constexpr uint32_t kBf16MaxFp16 = 0x477Fu;  // largest bf16 <= 65504
 
-__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
 
 // true when the direct path applied; w holds raw bf16 pairs
-__device__ __forceinline__ bool quant_int4_bf16(const uint32_t w[8], uint32_t q[2], uint16_t* scale) {
+__device__ __forceinline__ bool quant_int4_bf16(const uint32_t w[8], uint32_t q[2], uint16_t* scale,
+                                                const PackMul& mu) {
   const uint32_t ab = group_amax_bits(w);
   if (ab < 0x3B00u || ab > kBf16MaxFp16) return false;
   const __half sh = __float2half_rn(__fmul_rn(__uint_as_float(ab << 16), 1.0f / 7.0f));
   const float inv = __frcp_rn(__half2float(sh));
 #pragma unroll
   for (int k = 0; k < 2; ++k) {
-    uint32_t b[4];
+    float lo[4], hi[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
-      const uint32_t x = w[4 * k + j];
-      const uint32_t lo = round_bits(bf16_lo(x), inv), hi = round_bits(bf16_hi(x), inv) << 4;
-      b[j] = (lo & 0x0Fu) | (hi & 0xF0u);
+      lo[j] = __uint_as_float(w[4 * k + j] * mu.m64k);  // the low bf16 moved up: an IMAD, not an ALU shift
+      hi[j] = bf16_hi(w[4 * k + j]);
     }
-    q[k] = __byte_perm(__byte_perm(b[0], b[1], 0x0040), __byte_perm(b[2], b[3], 0x0040), 0x5410) ^ 0x88888888u;
+    q[k] = pack_int4_word(lo, hi, inv, mu);
   }
   *scale = __half_as_ushort(sh);
   return true;
 }
 
-__device__ __forceinline__ bool quant_int8_bf16(const uint32_t w[8], uint32_t q[4], uint16_t* scale) {
+__device__ __forceinline__ bool quant_int8_bf16(const uint32_t w[8], uint32_t q[4], uint16_t* scale,
+                                                const PackMul& mu) {
   const uint32_t ab = group_amax_bits(w);
   if (ab < 0x3D00u || ab > kBf16MaxFp16) return false;
   const __half sh = __float2half_rn(__fmul_rn(__uint_as_float(ab << 16), 1.0f / 127.0f));
@@ -346,9 +379,7 @@ __device__ __forceinline__ bool quant_int8_bf16(const uint32_t w[8], uint32_t q[
 #pragma unroll
   for (int k = 0; k < 4; ++k) {
     const uint32_t a = w[2 * k], b = w[2 * k + 1];
-    const uint32_t ab2 = __byte_perm(round_bits(bf16_lo(a), inv), round_bits(bf16_hi(a), inv), 0x0040);
-    const uint32_t cd = __byte_perm(round_bits(bf16_lo(b), inv), round_bits(bf16_hi(b), inv), 0x0040);
-    q[k] = __byte_perm(ab2, cd, 0x5410);
+    q[k] = pack_int8_word(__uint_as_float(a * mu.m64k), bf16_hi(a), __uint_as_float(b * mu.m64k), bf16_hi(b), inv, mu);
   }
   *scale = __half_as_ushort(sh);
   return true;

@@ -125,7 +125,7 @@ __device__ __forceinline__ void split_item(int it, const SectionTile& t, int& ve
 }
 
 template <int KIND, bool BF16, bool NEON>
-__device__ __forceinline__ void quantize_section(const SectionTile& t) {
+__device__ __forceinline__ void quantize_section(const SectionTile& t, const PackMul& mu) {
   const int items = t.tv * t.groups;
   for (int it = threadIdx.x; it < items; it += blockDim.x) {
     int vec, g;
@@ -144,24 +144,24 @@ __device__ __forceinline__ void quantize_section(const SectionTile& t) {
     } else if (KIND == kInt8) {
       uint32_t q[4];
       uint16_t sc;
-      if (NEON || !BF16 || !quant_int8_bf16(w, q, &sc)) {
+      if (NEON || !BF16 || !quant_int8_bf16(w, q, &sc, mu)) {
         if (BF16) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
         }
-        sc = NEON ? quant_int8_neon(w, q) : quant_int8(w, q);
+        sc = NEON ? quant_int8_neon(w, q) : quant_int8(w, q, mu);
       }
       *reinterpret_cast<uint4*>(qd + g * 16) = make_uint4(q[0], q[1], q[2], q[3]);
       *reinterpret_cast<uint16_t*>(t.sc + vec * t.s_bpv + g * 2) = sc;
     } else {
       uint32_t q[2];
       uint16_t sc;
-      if (NEON || !BF16 || !quant_int4_bf16(w, q, &sc)) {
+      if (NEON || !BF16 || !quant_int4_bf16(w, q, &sc, mu)) {
         if (BF16) {
 #pragma unroll
           for (int i = 0; i < 8; ++i) w[i] = bf16x2_to_f16x2(w[i]);
         }
-        sc = NEON ? quant_int4_neon(w, q) : quant_int4(w, q);
+        sc = NEON ? quant_int4_neon(w, q) : quant_int4(w, q, mu);
       }
       *reinterpret_cast<uint2*>(qd + g * 8) = make_uint2(q[0], q[1]);
       *reinterpret_cast<uint16_t*>(t.sc + vec * t.s_bpv + g * 2) = sc;
@@ -229,9 +229,9 @@ __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __gr
     const Section S = P.L.sec[s];
     const SectionTile st{(S.buf ? vp : kp) + v0 * P.head_dim + S.col, stage + P.stage_q[s], stage + P.stage_s[s],
                          P.head_dim, S.q_bpv, S.s_bpv, S.dim >> 4, P.gshift[s], tv};
-    if (S.kind == kInt4) quantize_section<kInt4, BF16, NEON>(st);
-    else if (S.kind == kInt8) quantize_section<kInt8, BF16, NEON>(st);
-    else quantize_section<kRaw, BF16, NEON>(st);
+    if (S.kind == kInt4) quantize_section<kInt4, BF16, NEON>(st, P.mul);
+    else if (S.kind == kInt8) quantize_section<kInt8, BF16, NEON>(st, P.mul);
+    else quantize_section<kRaw, BF16, NEON>(st, P.mul);
   }
 
   // header (32 bytes) by tile 0

@@ -43,6 +43,7 @@ struct EgressParams {
   int32_t gshift[3];        // log2(groups per row) of each section, -1 when not a power of two
   int32_t stage_bytes;
   int32_t neon_arith;       // quantize with the reference's ARM NEON fp16 arithmetic
+  PackMul mul;              // integer packing weights {16, 256, 65536}
 };
 
 struct MacParams {

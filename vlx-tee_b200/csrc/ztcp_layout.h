@@ -32,6 +32,12 @@ constexpr int kGroup = 16;
 
 enum SectionKind : int32_t { kRaw = 0, kInt8 = 1, kInt4 = 2 };
 
+// Integer weights of the quantizers' multiply-add packing (16, 256 and 65536), handed to the kernels as
+// parameters so that the compiler keeps each weighted sum as an integer multiply-add.
+struct PackMul {
+  uint32_t m16, m256, m64k;
+};
+
 struct Section {
   int32_t kind;    // SectionKind
   int32_t buf;     // 0 = K, 1 = V
