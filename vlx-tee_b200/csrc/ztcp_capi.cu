@@ -13,6 +13,9 @@
 #include "ztcp_kernels.cuh"
 #include "ztcp_layout.h"
 
+static_assert(sizeof(ztcp::IngressParams) <= 4096 && sizeof(ztcp::EgressParams) <= 4096,
+              "kernel parameter blocks must fit the classic 4 KB limit");
+
 namespace {
 
 thread_local std::string g_last_error;
@@ -145,6 +148,8 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
   P.n_tiles = (int32_t)((vecs + P.tile_vecs - 1) / P.tile_vecs);
   P.n_pages = batch->n_pages;
   P.stage_bytes = ztcp::plan_stage(P.L, P.tile_vecs, P.stage_q, P.stage_s);
+  ztcp::build_tile_plan(P.L, P.tile_vecs, P.stage_q, P.stage_s,
+                        (reinterpret_cast<uintptr_t>(P.out) | (uintptr_t)P.blob_stride) % 16 == 0, &P.plan);
   for (int i = 0; i < 3; ++i) {
     const int64_t groups = i < P.L.n ? P.L.sec[i].dim / ztcp::kGroup : 0;
     P.gshift[i] = (groups > 0 && (groups & (groups - 1)) == 0) ? __builtin_ctzll(groups) : -1;
@@ -259,6 +264,8 @@ int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_g
       const int i = (p - 1) * 3 + r;
       ztcp::build_layout(p, r, vecs, geom->head_dim, geom->rope_dim, has_v, &P.lay[i]);
       ztcp::plan_stage(P.lay[i], P.tile_vecs, P.lay_q[i], P.lay_s[i]);
+      ztcp::build_tile_plan(P.lay[i], P.tile_vecs, P.lay_q[i], P.lay_s[i],
+                            (reinterpret_cast<uintptr_t>(P.blobs) | (uintptr_t)P.blob_stride) % 16 == 0, &P.plan[i]);
     }
   if (P.n_pages * P.n_tiles > 0x7FFFFFFFLL) return fail(ZTCP_EINVAL, "batch too large for one launch");
 

@@ -102,6 +102,14 @@ __device__ __forceinline__ void xor_block_bytes(uint8_t* dst, const uint8_t* src
   }
 }
 
+// Range of flat block bi in a tile plan (ranges are few: compare against every boundary).
+__device__ __forceinline__ int plan_range(const TilePlan& T, int bi) {
+  int i = 0;
+#pragma unroll
+  for (int j = 1; j < 6; ++j) i += (j < T.n && bi >= T.first[j]) ? 1 : 0;
+  return i;
+}
+
 // One section's slice of a tile: source rows, staging areas and the (vec, group) index split.
 struct SectionTile {
   const uint16_t* src;  // first source element of the tile's first row in this section
@@ -216,7 +224,9 @@ __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __gr
   const int tile = (int)(blockIdx.x - page * P.n_tiles);
   const int64_t v0 = (int64_t)tile * P.tile_vecs;
   const int tv = (int)min((int64_t)P.tile_vecs, P.vecs - v0);
-  if (threadIdx.x == 0)
+  const bool padded = tile == P.n_tiles - 1 && P.payload_len > P.L.data_end;
+  const bool planned = P.plan.ok && tv == P.tile_vecs && !padded;
+  if (!planned && threadIdx.x == 0)
     build_range_table(T, P.L, v0, tv, P.stage_q, P.stage_s, tile == P.n_tiles - 1, P.payload_len);
   const int64_t blk = page_block(P.meta, page);
   const uint16_t* kp = P.k + blk * P.page_elems;
@@ -259,9 +269,28 @@ __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __gr
   __syncthreads();
 
   // ---- phase 2: encrypt this tile's byte ranges
-  const int64_t total_blocks = T.first[T.n];
   const uint32_t n2 = ((uint32_t)layer << 16) | P.meta.head_group;
   uint8_t* payload = blob + kHeaderBytes;
+  if (planned) {  // whole, 16-byte aligned blocks
+    const int total = P.plan.first[P.plan.n];
+    for (int bi = threadIdx.x; bi < total; bi += blockDim.x) {
+      const int i = plan_range(P.plan, bi);
+      const int rel = bi - P.plan.first[i];
+      const int kb = P.plan.kb0[i] + tile * (P.plan.first[i + 1] - P.plan.first[i]) + rel;
+      uint32_t ks[16];
+      chacha20_block(P.key, (uint32_t)(1 + kb), (uint32_t)seq, (uint32_t)(seq >> 32), n2, ks);
+      const uint4* src = reinterpret_cast<const uint4*>(stage + P.plan.stage[i] + rel * 64);
+      uint4* dst = reinterpret_cast<uint4*>(payload + (int64_t)kb * 64);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint4 pt = src[w];
+        pt.x ^= ks[4 * w]; pt.y ^= ks[4 * w + 1]; pt.z ^= ks[4 * w + 2]; pt.w ^= ks[4 * w + 3];
+        dst[w] = pt;
+      }
+    }
+    return;
+  }
+  const int64_t total_blocks = T.first[T.n];
   for (int64_t bi = threadIdx.x; bi < total_blocks; bi += blockDim.x) {
     const int i = find_range(T, bi);
     const Range r = T.r[i];
@@ -492,41 +521,64 @@ __global__ void __launch_bounds__(kTileThreads, 6) ingress_tile_kernel(const __g
   const Layout& L = P.lay[li];
   const int32_t* sq = P.lay_q[li];
   const int32_t* ss = P.lay_s[li];
-  if (threadIdx.x == 0) build_range_table(T, L, v0, tv, sq, ss, false, P.payload_len);
-  __syncthreads();
-
-  // ---- phase 1: decrypt this tile's byte ranges into shared memory (loads issued before the keystream)
-  const int64_t total_blocks = T.first[T.n];
+  const TilePlan& TP = P.plan[li];
+  const bool planned = TP.ok && tv == P.tile_vecs;
   const uint32_t n0 = h6, n1 = h7, n2 = (h3 << 16) | (h3 >> 16);
   const uint8_t* payload = blob + kHeaderBytes;
-  for (int64_t bi = threadIdx.x; bi < total_blocks; bi += blockDim.x) {
-    const int i = find_range(T, bi);
-    const Range r = T.r[i];
-    const int64_t kb = (r.a >> 6) + (bi - T.first[i]);
-    uint32_t ks[16];
-    const int64_t base = kb << 6;
-    const int lo = (int)(max(r.a, base) - base), hi = (int)(min(r.b, base + 64) - base);
-    const uint8_t* src = payload + base;
-    uint8_t* dst = stage + r.stage + (base - r.a);  // only bytes [lo, hi) are written
-    if (lo == 0 && hi == 64 &&
-        ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+
+  // ---- phase 1: decrypt this tile's byte ranges into shared memory (loads issued before the keystream)
+  if (planned) {  // whole, 16-byte aligned blocks
+    const int total = TP.first[TP.n];
+    for (int bi = threadIdx.x; bi < total; bi += blockDim.x) {
+      const int i = plan_range(TP, bi);
+      const int rel = bi - TP.first[i];
+      const int kb = TP.kb0[i] + tile * (TP.first[i + 1] - TP.first[i]) + rel;
+      const uint4* src = reinterpret_cast<const uint4*>(payload + (int64_t)kb * 64);
       uint4 c[4];
 #pragma unroll
-      for (int w = 0; w < 4; ++w) c[w] = __ldg(reinterpret_cast<const uint4*>(src) + w);
+      for (int w = 0; w < 4; ++w) c[w] = __ldg(src + w);
+      uint32_t ks[16];
       chacha20_block(P.key, (uint32_t)(1 + kb), n0, n1, n2, ks);
+      uint4* dst = reinterpret_cast<uint4*>(stage + TP.stage[i] + rel * 64);
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
         c[w].x ^= ks[4 * w]; c[w].y ^= ks[4 * w + 1]; c[w].z ^= ks[4 * w + 2]; c[w].w ^= ks[4 * w + 3];
-        reinterpret_cast<uint4*>(dst)[w] = c[w];
+        dst[w] = c[w];
       }
-    } else {
-      chacha20_block(P.key, (uint32_t)(1 + kb), n0, n1, n2, ks);
+    }
+  } else {
+    if (threadIdx.x == 0) build_range_table(T, L, v0, tv, sq, ss, false, P.payload_len);
+    __syncthreads();
+    const int64_t total_blocks = T.first[T.n];
+    for (int64_t bi = threadIdx.x; bi < total_blocks; bi += blockDim.x) {
+      const int i = find_range(T, bi);
+      const Range r = T.r[i];
+      const int64_t kb = (r.a >> 6) + (bi - T.first[i]);
+      uint32_t ks[16];
+      const int64_t base = kb << 6;
+      const int lo = (int)(max(r.a, base) - base), hi = (int)(min(r.b, base + 64) - base);
+      const uint8_t* src = payload + base;
+      uint8_t* dst = stage + r.stage + (base - r.a);  // only bytes [lo, hi) are written
+      if (lo == 0 && hi == 64 &&
+          ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0) {
+        uint4 c[4];
 #pragma unroll
-      for (int w = 0; w < 16; ++w) {
+        for (int w = 0; w < 4; ++w) c[w] = __ldg(reinterpret_cast<const uint4*>(src) + w);
+        chacha20_block(P.key, (uint32_t)(1 + kb), n0, n1, n2, ks);
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int x = 4 * w + j;
-          if (x >= lo && x < hi) dst[x] = (uint8_t)(src[x] ^ (uint8_t)(ks[w] >> (8 * j)));
+        for (int w = 0; w < 4; ++w) {
+          c[w].x ^= ks[4 * w]; c[w].y ^= ks[4 * w + 1]; c[w].z ^= ks[4 * w + 2]; c[w].w ^= ks[4 * w + 3];
+          reinterpret_cast<uint4*>(dst)[w] = c[w];
+        }
+      } else {
+        chacha20_block(P.key, (uint32_t)(1 + kb), n0, n1, n2, ks);
+#pragma unroll
+        for (int w = 0; w < 16; ++w) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int x = 4 * w + j;
+            if (x >= lo && x < hi) dst[x] = (uint8_t)(src[x] ^ (uint8_t)(ks[w] >> (8 * j)));
+          }
         }
       }
     }

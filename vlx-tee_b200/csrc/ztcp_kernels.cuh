@@ -22,6 +22,19 @@ struct PageMeta {
 
 constexpr int kTileThreads = 256;
 
+// Keystream work of a full tile when every byte range it owns is whole 64-byte blocks (true for the
+// standard geometries): range i covers the tile's blocks [first[i], first[i+1]), starting at keystream block
+// kb0[i] + tile * (first[i+1] - first[i]), with its plaintext at staging offset stage[i].  Built on the host,
+// so a CTA maps a block to its range by comparisons instead of a table that one thread builds while the
+// others wait.  ok == 0: the kernels take the general path (ragged or unaligned ranges, padded tails).
+struct TilePlan {
+  int32_t ok;
+  int32_t n;
+  int32_t first[7];
+  int32_t kb0[6];
+  int32_t stage[6];
+};
+
 struct EgressParams {
   const uint16_t* k;        // KV pool (fp16 or bf16 bits), page p at k + kv_block[p] * page_elems
   const uint16_t* v;        // null for a single-buffer MLA page
@@ -44,6 +57,7 @@ struct EgressParams {
   int32_t stage_bytes;
   int32_t neon_arith;       // quantize with the reference's ARM NEON fp16 arithmetic
   PackMul mul;              // integer packing weights {16, 256, 65536}
+  TilePlan plan;            // full tiles of L (blobs 16-byte aligned)
 };
 
 struct MacParams {
@@ -85,6 +99,7 @@ struct IngressParams {
   Layout lay[9];
   int32_t lay_q[9][3];
   int32_t lay_s[9][3];
+  TilePlan plan[9];         // full tiles of each layout (blobs 16-byte aligned)
 };
 
 void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream);
@@ -106,6 +121,33 @@ ZTCP_HD int32_t plan_stage(const Layout& L, int32_t tile_vecs, int32_t stage_q[3
     off += ((int64_t)tile_vecs * L.sec[i].s_bpv + 15) / 16 * 16;
   }
   return (int32_t)off;
+}
+
+// Tile plan of a layout for full tiles of tile_vecs vecs (see TilePlan); ok stays 0 when a range is not whole
+// 64-byte blocks, block indices would not fit 32 bits, or aligned is false (blobs not 16-byte aligned).
+ZTCP_HD void build_tile_plan(const Layout& L, int32_t tile_vecs, const int32_t stage_q[3], const int32_t stage_s[3],
+                             bool aligned, TilePlan* T) {
+  T->ok = 0;
+  T->n = 0;
+  int64_t acc = 0;
+  bool good = aligned;
+  for (int i = 0; i < L.n && i < 3; ++i) {
+    const Section& S = L.sec[i];
+    for (int part = 0; part < 2; ++part) {
+      if (part == 1 && S.kind == kRaw) break;
+      const int64_t a0 = part == 0 ? S.q_off : S.s_off;
+      const int64_t bytes = (int64_t)tile_vecs * (part == 0 ? S.q_bpv : S.s_bpv);
+      if (a0 % 64 != 0 || bytes % 64 != 0 || bytes == 0 || a0 / 64 > 0x3FFFFFFF) good = false;
+      T->first[T->n] = (int32_t)acc;
+      T->kb0[T->n] = (int32_t)(a0 / 64);
+      T->stage[T->n] = part == 0 ? stage_q[i] : stage_s[i];
+      acc += bytes / 64;
+      ++T->n;
+    }
+  }
+  T->first[T->n] = (int32_t)acc;
+  if (L.data_end / 64 > 0x3FFFFFFF) good = false;
+  T->ok = good && T->n > 0 ? 1 : 0;
 }
 
 }  // namespace ztcp
