@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 #include "ztcp_device.cuh"
 #include "ztcp_kernels.cuh"
 
@@ -668,13 +670,18 @@ void launch_mac(const MacParams& P, bool verify, cudaStream_t stream) {
   // running concurrently on another stream -- is co-scheduled on its sub-partitions.
   static_assert(kRingBytes <= kMacReserveBytes, "chain rings must fit the reserved shared memory");
   const unsigned grid = (unsigned)((P.n_pages + kChainThreads - 1) / kChainThreads);
-  if (verify) {
-    cudaFuncSetAttribute(mac_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMacReserveBytes);
-    mac_kernel<true><<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
-  } else {
-    cudaFuncSetAttribute(mac_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMacReserveBytes);
-    mac_kernel<false><<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
+  // the shared-memory opt-in is a per-device property of each kernel: set it on a device's first launch
+  static std::atomic<uint64_t> opted[2];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
+  if (!bit || !(opted[verify].load(std::memory_order_relaxed) & bit)) {
+    if (verify) cudaFuncSetAttribute(mac_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMacReserveBytes);
+    else cudaFuncSetAttribute(mac_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMacReserveBytes);
+    opted[verify].fetch_or(bit, std::memory_order_relaxed);
   }
+  if (verify) mac_kernel<true><<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
+  else mac_kernel<false><<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
 }
 
 void launch_ingress(const IngressParams& P, cudaStream_t stream) {

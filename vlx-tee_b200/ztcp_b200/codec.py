@@ -18,8 +18,23 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+# The current stream's raw handle without building a torch.cuda.Stream object (the lookup torch's own
+# kernels use); the public call is the fallback.
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream_handle(device: torch.device) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device.index)
     return torch.cuda.current_stream(device).cuda_stream
+
+
+def _on_device(device: torch.device, fn, *args):
+    """Call fn(*args) with `device` current (the C-ABI launches on the current device)."""
+    if torch.cuda.current_device() == device.index:
+        return fn(*args)
+    with torch.cuda.device(device):
+        return fn(*args)
 
 
 def _require_cuda(name: str, t: torch.Tensor, dtypes, device: torch.device | None = None) -> None:
@@ -27,7 +42,7 @@ def _require_cuda(name: str, t: torch.Tensor, dtypes, device: torch.device | Non
         raise RuntimeError(f"{name} must be a torch.Tensor")
     if not t.is_cuda:
         raise RuntimeError(f"{name} must be a CUDA tensor")
-    if device is not None and t.device != device:
+    if device is not None and t.get_device() != device.index:
         raise RuntimeError(f"{name} must be on {device}, got {t.device}")
     if not t.is_contiguous():
         raise RuntimeError(f"{name} must be contiguous")
@@ -36,19 +51,11 @@ def _require_cuda(name: str, t: torch.Tensor, dtypes, device: torch.device | Non
 
 
 def _page_batch(n_pages: int, token_hashes: torch.Tensor, block_table, sequence_nonces, layer_ids,
-                base_sequence_nonce: int, tenant: int, model: int, layer_id: int, head_group: int) -> capi.PageBatch:
-    b = capi.PageBatch()
-    b.n_pages = n_pages
-    b.kv_block = _ptr(block_table)
-    b.token_hash = _ptr(token_hashes)
-    b.sequence_nonce = _ptr(sequence_nonces)
-    b.layer_id = _ptr(layer_ids)
-    b.base_sequence_nonce = int(base_sequence_nonce) & _U64
-    b.tenant_id_hash = int(tenant) & 0xFFFFFFFF
-    b.model_id_hash = int(model) & 0xFFFFFFFF
-    b.layer_id_uniform = int(layer_id) & 0xFFFF
-    b.head_group_id = int(head_group) & 0xFFFF
-    return b
+                base_sequence_nonce: int, tenant: int, model: int, layer_id: int, head_group: int,
+                options: int = 0) -> capi.PageBatch:
+    return capi.PageBatch(n_pages, _ptr(block_table), token_hashes.data_ptr(), _ptr(sequence_nonces), _ptr(layer_ids),
+                          int(base_sequence_nonce) & _U64, int(tenant) & 0xFFFFFFFF, int(model) & 0xFFFFFFFF,
+                          int(layer_id) & 0xFFFF, int(head_group) & 0xFFFF, options)
 
 
 def _check_meta(dev, n, block_table, sequence_nonces, layer_ids, token_hashes):
@@ -111,13 +118,12 @@ def encode_pages(k_pool: torch.Tensor, v_pool: torch.Tensor | None, token_hashes
     _, T, H, D = k_pool.shape
     geom = capi.geometry(T, H, D, rope_dim, v_pool is None)
     batch = _page_batch(n, token_hashes, block_table, sequence_nonces, layer_ids, base_sequence_nonce,
-                        tenant_id_hash, model_id_hash, layer_id, head_group_id)
-    batch.options = capi.OPT_NEON_ARITH if neon_arith else 0
+                        tenant_id_hash, model_id_hash, layer_id, head_group_id,
+                        capi.OPT_NEON_ARITH if neon_arith else 0)
     dtype = capi.DTYPE_BF16 if k_pool.dtype == torch.bfloat16 else capi.DTYPE_F16
-    lib = capi.load()
-    with torch.cuda.device(dev):
-        rc = lib.ztcp_encode_pages(_ptr(k_pool), _ptr(v_pool), dtype, geom, batch, int(preset), int(rope_mode),
-                                   int(expected_payload_bytes), keys, _ptr(out_blobs), _stream_handle(dev))
+    rc = _on_device(dev, capi.load().ztcp_encode_pages, k_pool.data_ptr(), _ptr(v_pool), dtype, geom, batch,
+                    int(preset), int(rope_mode), int(expected_payload_bytes), keys, out_blobs.data_ptr(),
+                    _stream_handle(dev))
     capi.check(rc)
 
 
@@ -156,10 +162,8 @@ def decode_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, out_k: torch.T
     geom = capi.geometry(T, H, D, rope_dim, is_mla)
     batch = _page_batch(n, token_hashes, block_table, None, layer_ids, 0, tenant_id_hash, model_id_hash,
                         layer_id, 0)
-    lib = capi.load()
-    with torch.cuda.device(dev):
-        rc = lib.ztcp_decode_pages(_ptr(blobs), int(blob_bytes), geom, batch, keys, _ptr(out_k), _ptr(out_v),
-                                   _ptr(status), _ptr(any_fail), _stream_handle(dev))
+    rc = _on_device(dev, capi.load().ztcp_decode_pages, blobs.data_ptr(), int(blob_bytes), geom, batch, keys,
+                    out_k.data_ptr(), _ptr(out_v), status.data_ptr(), any_fail.data_ptr(), _stream_handle(dev))
     capi.check(rc)
     return status, any_fail
 
@@ -181,9 +185,8 @@ def verify_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, *, num_tokens:
         any_fail = torch.empty(1, dtype=torch.int32, device=dev)
     geom = capi.geometry(num_tokens, num_heads, head_dim, rope_dim, is_mla)
     batch = _page_batch(n, token_hashes, None, None, layer_ids, 0, tenant_id_hash, model_id_hash, layer_id, 0)
-    with torch.cuda.device(dev):
-        rc = capi.load().ztcp_verify_pages(_ptr(blobs), int(blob_bytes), geom, batch, keys, _ptr(status),
-                                           _ptr(any_fail), _stream_handle(dev))
+    rc = _on_device(dev, capi.load().ztcp_verify_pages, blobs.data_ptr(), int(blob_bytes), geom, batch, keys,
+                    status.data_ptr(), any_fail.data_ptr(), _stream_handle(dev))
     capi.check(rc)
     return status, any_fail
 
