@@ -73,6 +73,11 @@ typedef struct ztcp_keys {
  * options: ZTCP_OPT_* bits (0 = the reference's scalar x86-64 arithmetic, bit-exact with its build). */
 #define ZTCP_OPT_NEON_ARITH 1 /* egress: quantize with the reference's ARM NEON fp16 arithmetic (its build with
                                  __ARM_FEATURE_FP16_VECTOR_ARITHMETIC, csrc:718-733 / :786-803); decode ignores it */
+#define ZTCP_OPT_PAGE_FALLBACK 2 /* decode: zero only the pages that fail (status != 0) and decode the others,
+                                    for a caller that recomputes failed pages instead of dropping the batch
+                                    (the per-page fallback of the reference's design, paper main.tex:174);
+                                    without it any failing page zeroes every output page, as the reference's
+                                    decoders do (csrc:2481-2495).  any_fail is set either way; egress ignores it */
 typedef struct ztcp_page_batch {
   int64_t n_pages;
   const int32_t* kv_block;

@@ -47,7 +47,7 @@ int32_t check_batch(const ztcp_page_batch* b) {
   if (!b) return fail(ZTCP_EINVAL, "page batch must not be NULL");
   if (b->n_pages <= 0) return fail(ZTCP_EINVAL, "batch must hold at least one page");
   if (!b->token_hash) return fail(ZTCP_EINVAL, "page_token_hashes must not be NULL");
-  if (b->options & ~ZTCP_OPT_NEON_ARITH) return fail(ZTCP_EINVAL, "unknown page batch options");
+  if (b->options & ~(ZTCP_OPT_NEON_ARITH | ZTCP_OPT_PAGE_FALLBACK)) return fail(ZTCP_EINVAL, "unknown page batch options");
   return ZTCP_OK;
 }
 
@@ -251,6 +251,8 @@ int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_g
   P.meta = to_meta(batch);
   key_words(keys, P.key);
   P.any_fail = any_fail;
+  P.status = status;
+  P.page_fallback = (batch->options & ZTCP_OPT_PAGE_FALLBACK) != 0;
   const int64_t worst = ztcp::worst_stage_bytes_per_vec(geom->head_dim, geom->rope_dim, has_v);
   P.tile_vecs = pick_tile_vecs(vecs, worst);
   P.n_tiles = (int32_t)((vecs + P.tile_vecs - 1) / P.tile_vecs);

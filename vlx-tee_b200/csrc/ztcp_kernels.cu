@@ -5,7 +5,7 @@
 // Ingress = mac_kernel<verify>  (header / AAD / tag / flags checks, per-page status, batch fail flag)
 //         + ingress_tile_kernel (decrypt + dequantize per (page, vec-tile); zeroes every output when
 //                                any page of the batch failed -- the reference's all-or-nothing rule,
-//                                csrc:2481-2495)
+//                                csrc:2481-2495 -- or, with the page-fallback option, only the failed pages)
 //
 // Tiling.  A CTA owns `tile_vecs` consecutive vecs (token x head rows) of one page.  Those rows map
 // to one contiguous byte range per q region and per scale region of every section (the payload is
@@ -495,7 +495,7 @@ __global__ void __launch_bounds__(kTileThreads, 6) ingress_tile_kernel(const __g
   uint16_t* kd = P.k_out + blk * P.page_elems;
   uint16_t* vd = P.v_out ? P.v_out + blk * P.page_elems : nullptr;
 
-  if (*P.any_fail != 0) {
+  if (P.page_fallback ? P.status[page] != 0 : *P.any_fail != 0) {
     const int64_t n16 = (int64_t)tv * P.head_dim / 8;  // uint4 per buffer
     uint4* kz = reinterpret_cast<uint4*>(kd + v0 * P.head_dim);
     uint4* vz = vd ? reinterpret_cast<uint4*>(vd + v0 * P.head_dim) : nullptr;

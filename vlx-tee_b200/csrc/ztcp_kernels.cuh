@@ -90,6 +90,8 @@ struct IngressParams {
   PageMeta meta;
   uint32_t key[8];
   const int32_t* any_fail;
+  const int32_t* status;     // per-page verify status (read when page_fallback)
+  int32_t page_fallback;     // zero only failing pages instead of the whole batch
   int32_t tile_vecs;
   int32_t n_tiles;
   int64_t n_pages;

@@ -7,6 +7,7 @@ Modules:
   cold_page_spec -- wire-format spec mirror (header, presets, geometry, payload sizes)
   session        -- GPU-native session codec: the reference wrapper's six methods on CUDA tensors
   offload        -- egress to / ingress from pinned host memory with copies overlapped across slots
+  hooks          -- engine offload hooks: pinned staging ring, page codec with a per-page recompute fallback
   keyring        -- session keyring with the reference's interface, per-page tables in the C++ ledger
   ledger         -- ctypes binding of the ledger C-ABI (include/ztcp_ledger.h)
   errors         -- exception classes with the reference's names and hierarchy
@@ -16,5 +17,5 @@ Modules:
 """
 from . import build, capi, cold_page_spec  # noqa: F401
 
-__all__ = ["build", "capi", "cold_page_spec", "codec", "errors", "fused_ext", "keyring", "ledger", "offload",
+__all__ = ["build", "capi", "cold_page_spec", "codec", "errors", "fused_ext", "hooks", "keyring", "ledger", "offload",
            "session", "sharding", "workload"]

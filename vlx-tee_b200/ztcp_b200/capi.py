@@ -70,6 +70,7 @@ class PageBatch(C.Structure):
 
 
 OPT_NEON_ARITH = 1
+OPT_PAGE_FALLBACK = 2
 
 
 class ZtcpError(RuntimeError):

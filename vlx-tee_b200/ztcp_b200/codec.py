@@ -131,11 +131,13 @@ def decode_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, out_k: torch.T
                  out_v: torch.Tensor | None, *, rope_dim: int, is_mla: bool, tenant_id_hash: int,
                  model_id_hash: int, layer_id: int, keys: capi.Keys, block_table: torch.Tensor | None = None,
                  layer_ids: torch.Tensor | None = None, status: torch.Tensor | None = None,
-                 any_fail: torch.Tensor | None = None, check_block_table: bool = True):
+                 any_fail: torch.Tensor | None = None, check_block_table: bool = True,
+                 page_fallback: bool = False):
     """Ingress of ``blobs.shape[0]`` pages into fp16 pools [pool_pages, T, H, D].
 
     Enqueues verify + decrypt; returns the device tensors (status[n] int32, any_fail[1] int32).  When
-    any page fails, every output page of the batch is zeroed.
+    any page fails, every output page of the batch is zeroed -- or, with ``page_fallback``, only the pages
+    whose status is non-zero (the others are decoded).
     """
     dev = blobs.device
     _require_cuda("cold_blobs", blobs, (torch.uint8,))
@@ -161,7 +163,7 @@ def decode_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, out_k: torch.T
     _, T, H, D = out_k.shape
     geom = capi.geometry(T, H, D, rope_dim, is_mla)
     batch = _page_batch(n, token_hashes, block_table, None, layer_ids, 0, tenant_id_hash, model_id_hash,
-                        layer_id, 0)
+                        layer_id, 0, capi.OPT_PAGE_FALLBACK if page_fallback else 0)
     rc = _on_device(dev, capi.load().ztcp_decode_pages, blobs.data_ptr(), int(blob_bytes), geom, batch, keys,
                     out_k.data_ptr(), _ptr(out_v), status.data_ptr(), any_fail.data_ptr(), _stream_handle(dev))
     capi.check(rc)

@@ -203,6 +203,68 @@ class ColdPageCodec:
                 out_v.zero_()
             raise
 
+    def decode_cold_pages_partial(self, cold_blobs_u8: torch.Tensor, expected_token_hashes_i64: torch.Tensor,
+                                  out_k_pages: torch.Tensor, out_v_pages: torch.Tensor | None,
+                                  expected_tenant_id: str, session_id: str, expected_model_id: str,
+                                  expected_layer_id: int, min_sequence_nonce: int | None = None) -> torch.Tensor:
+        """Batch ingress with a per-page fallback: returns a CPU bool tensor, True for each page decoded into
+        the outputs, False for each page that failed its header, AAD, MAC, flags or freshness check (its
+        outputs are zeroed and its slot watermark is left as it was).  A session-level failure (the key
+        shredded before or during the call) still raises, with every output zeroed.  This is the per-page
+        recovery the reference's design describes for an engine's offload hook (paper main.tex:174); the
+        reference's own decoders are all-or-nothing (``decode_cold_pages_peak_into``)."""
+        if (_overlap(out_k_pages, out_v_pages) or _overlap(out_k_pages, cold_blobs_u8)
+                or _overlap(out_v_pages, cold_blobs_u8)):
+            raise RuntimeError("Peak ingress output tensors must not alias or overlap each other or input tensors")
+        tenant_id = expected_tenant_id
+        gen, enc_key, mac_key = self.keyring.begin_ingress(tenant_id, session_id)
+        out_k, out_v = out_k_pages, out_v_pages
+        try:
+            toks_dev, toks_host = self._token_hashes(expected_token_hashes_i64)
+            n = toks_host.size
+            if cold_blobs_u8.dim() != 2 or cold_blobs_u8.shape[0] != n or cold_blobs_u8.dtype != torch.uint8:
+                raise RuntimeError(f"cold blobs must be uint8 [batch, blob_bytes] with batch={n}, got "
+                                   f"{tuple(cold_blobs_u8.shape)} {cold_blobs_u8.dtype}")
+            self._check_pages(out_k, out_v, n, "output")
+            bd = self._dev(cold_blobs_u8.contiguous())
+            kd = out_k if out_k.device == self.device else torch.empty(out_k.shape, dtype=torch.float16,
+                                                                         device=self.device)
+            vd = None if out_v is None else (out_v if out_v.device == self.device else
+                                             torch.empty(out_v.shape, dtype=torch.float16, device=self.device))
+            status, _ = codec.decode_pages(bd, toks_dev, kd, vd, rope_dim=self.geometry.rope_dim,
+                                           is_mla=bool(self.geometry.is_mla_single_buffer),
+                                           tenant_id_hash=hash32(tenant_id), model_id_hash=hash32(expected_model_id),
+                                           layer_id=expected_layer_id, keys=_keys(enc_key, mac_key),
+                                           page_fallback=True)
+            hits = (status == 0).cpu()
+            records = ledger.records_from_headers(bd[:, :HEADER_BYTES].cpu().numpy())
+            for i in np.flatnonzero(hits.numpy()):
+                r = records[i]
+                try:
+                    self.keyring.verify_and_update_freshness(
+                        tenant_id=tenant_id, session_id=session_id, model_id_hash=int(r["model_id_hash"]),
+                        layer_id=int(r["layer_id"]), head_group_id=int(r["head_group_id"]),
+                        page_token_hash=int(r["page_token_hash"]), sequence_nonce=int(r["sequence_nonce"]),
+                        min_sequence_nonce=min_sequence_nonce, expected_generation=gen)
+                except self.errors.StalePageReplayError:
+                    hits[i] = False
+            misses = torch.nonzero(~hits).flatten().to(self.device)
+            if misses.numel():
+                kd.index_fill_(0, misses, 0)
+                if vd is not None:
+                    vd.index_fill_(0, misses, 0)
+            self.keyring.finish_ingress(tenant_id, session_id, gen)
+            if kd is not out_k:
+                out_k.copy_(kd)
+            if vd is not None and vd is not out_v:
+                out_v.copy_(vd)
+            return hits
+        except BaseException:
+            out_k.zero_()
+            if out_v is not None:
+                out_v.zero_()
+            raise
+
     def decode_cold_pages_peak_into(self, cold_blobs_u8: torch.Tensor, expected_token_hashes_i64: torch.Tensor,
                                     out_k_pages: torch.Tensor, out_v_pages: torch.Tensor | None,
                                     expected_tenant_id: str, session_id: str, expected_model_id: str,
