@@ -57,7 +57,7 @@ def parse_args():
     ap.add_argument("--pages", type=int, default=256, help="pages per GPU per step")
     ap.add_argument("--sets", type=int, default=4, help="input sets (rounded up to a multiple of --inflight)")
     ap.add_argument("--inflight", type=int, default=32, help="batches in flight (CUDA streams)")
-    ap.add_argument("--e2e-steps", type=int, default=64)
+    ap.add_argument("--e2e-steps", type=int, default=256)
     ap.add_argument("--e2e-inflight", type=int, default=8,
                     help="batches in flight in the end-to-end run (host<->device copies are link-bound; a few "
                          "streams keep both copy directions busy)")
