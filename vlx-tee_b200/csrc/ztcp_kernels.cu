@@ -381,39 +381,30 @@ __device__ __forceinline__ void siphash_bytes(SipState& st, const uint8_t* p, in
     for (int c = 0; c < kRing - 1; ++c) ring_fill(ring, p, c, n_chunks);
     const W64 after = n_chunks * 16 < n_words ? load_word_any(p + n_chunks * kChunk) : fin;
     cp_async_wait<kRing - 2>();  // chunk 0 landed
-    uint4 A[8], B[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) A[j] = slot(0)[j];
-    st.v3 = xor64(st.v3, W64{A[0].x, A[0].y});
-    // Chunk c is in registers when iteration c starts; the iteration refills the ring, waits for chunk
-    // c+1, reads it into the other register buffer (its latency hidden by absorbing chunk c) and
-    // absorbs chunk c, whose last word looks ahead into chunk c+1.
-    auto absorb_chunk = [&](const uint4 (&X)[8], W64 nx) {
+    st.v3 = xor64(st.v3, load_word_any(p));  // word 0
+    // Chunk c is read from the ring a 16-byte pair at a time right before its words are absorbed (the
+    // shared-memory loads hide under the previous word's rounds); its last word looks ahead into chunk
+    // c+1, which has landed too.  (Staging each chunk through two 8 x uint4 register buffers instead was
+    // measured 4.5 % slower: 100.2 vs 95.7 cycles/word.)
+#pragma unroll 1
+    for (int64_t c = 0; c < n_chunks; ++c) {
+      ring_fill(ring, p, c + kRing - 1, n_chunks);
+      cp_async_wait<kRing - 2>();  // chunks c and c+1 landed
+      const uint4* w = slot(c);
+      const W64 last = c + 1 < n_chunks ? W64{slot(c + 1)[0].x, slot(c + 1)[0].y} : after;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        st.absorb_pre(W64{X[j].x, X[j].y}, W64{X[j].z, X[j].w});
-        st.absorb_pre(W64{X[j].z, X[j].w}, j < 7 ? W64{X[j + 1].x, X[j + 1].y} : nx);
+        const uint4 q = w[j];
+        st.absorb_pre(W64{q.x, q.y}, W64{q.z, q.w});
+        W64 nx;
+        if (j < 7) {
+          const uint4 r = w[j + 1];
+          nx = W64{r.x, r.y};
+        } else {
+          nx = last;
+        }
+        st.absorb_pre(W64{q.z, q.w}, nx);
       }
-    };
-#pragma unroll 1
-    for (int64_t c = 0; c < n_chunks; c += 2) {
-      ring_fill(ring, p, c + kRing - 1, n_chunks);
-      cp_async_wait<kRing - 2>();  // chunk c+1 landed
-      const bool has1 = c + 1 < n_chunks;
-      if (has1) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) B[j] = slot(c + 1)[j];
-      }
-      absorb_chunk(A, has1 ? W64{B[0].x, B[0].y} : after);
-      if (!has1) break;
-      ring_fill(ring, p, c + kRing, n_chunks);
-      cp_async_wait<kRing - 2>();  // chunk c+2 landed
-      const bool has2 = c + 2 < n_chunks;
-      if (has2) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) A[j] = slot(c + 2)[j];
-      }
-      absorb_chunk(B, has2 ? W64{A[0].x, A[0].y} : after);
     }
     cp_async_wait<0>();
     i0 = n_chunks * 16;
