@@ -475,3 +475,52 @@ def test_neon_arithmetic_option(ext, oracle, mla):
                 okd, ovd, _, first = helpers.oracle_decode(oracle, want, toks, k16.shape, rope, mla, m)
                 assert first == -1
                 np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd, err_msg=tag)
+
+
+def test_round_trip_replays_from_a_cuda_graph(ext, oracle):
+    """The C-ABI neither allocates nor synchronizes, so an egress + ingress round trip can be captured in a
+    CUDA graph and replayed (a launch-bound caller's way to cut host time); replays write the oracle's bytes."""
+    from ztcp_b200 import capi, codec, workload
+
+    n = 16
+    m = workload.session_material(91)
+    k32, v32 = workload.kv_pages_np(n, workload.GQA, seed=92)
+    k = torch.from_numpy(k32).to(torch.bfloat16).to(DEV)
+    v = torch.from_numpy(v32).to(torch.bfloat16).to(DEV)
+    toks_np = workload.token_hashes(n, 93)
+    toks = torch.from_numpy(toks_np.view(np.int64)).to(DEV)
+    keys = capi.keys(*m["key"], *m["mac_key"])
+    blobs = torch.zeros((n, 98352), dtype=torch.uint8, device=DEV)
+    ko = torch.zeros((n, 64, 8, 128), dtype=torch.float16, device=DEV)
+    vo = torch.zeros_like(ko)
+    st = torch.empty(n, dtype=torch.int32, device=DEV)
+    fl = torch.empty(1, dtype=torch.int32, device=DEV)
+
+    def round_trip():
+        codec.encode_pages(k, v, toks, blobs, rope_dim=64, preset=1, rope_mode=1, expected_payload_bytes=98304,
+                           tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"],
+                           head_group_id=m["head_group"], base_sequence_nonce=m["base_seq"], keys=keys)
+        codec.decode_pages(blobs, toks, ko, vo, rope_dim=64, is_mla=False, tenant_id_hash=m["tenant"],
+                           model_id_hash=m["model"], layer_id=m["layer"], keys=keys, status=st, any_fail=fl)
+
+    side = torch.cuda.Stream(DEV)
+    with torch.cuda.stream(side):
+        round_trip()  # first launches (per-device kernel attributes) outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        round_trip()
+    want = helpers.oracle_encode(oracle, k.cpu().half().numpy(), v.cpu().half().numpy(), toks_np, 64, 1, 1, 98304, m)
+    okd, ovd, _, first = helpers.oracle_decode(oracle, want, toks_np, (n, 64, 8, 128), 64, False, m)
+    assert first == -1
+    for _ in range(3):
+        blobs.zero_()
+        ko.zero_()
+        vo.zero_()
+        g.replay()
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(blobs.cpu().numpy(), want)
+        assert int(fl.item()) == 0
+        np.testing.assert_array_equal(ko.cpu().numpy().view(np.uint16), okd)
+        np.testing.assert_array_equal(vo.cpu().numpy().view(np.uint16), ovd)
+    del g
