@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """ZTCP cold-page codec benchmark on B200 -- prints one JSON line (rank 0).
 
-Workload: BASELINE configuration 0 -- a batch of 256 GQA pages (64 tokens x 8 KV heads x 128, separate
+Workload: the reference's headline configuration (its benchmark's config 0) -- a batch of 256 GQA pages (64 tokens x 8 KV heads x 128, separate
 K and V in bf16, 256 KiB hot per page), INT4_SYM + PRESERVE_FP8, N(0,1) values with four x15 RoPE
 outlier channels per head, random 256-bit ChaCha20 key, 128-bit SipHash key and 64-bit base nonce.
 One step = egress (quantize, pack, encrypt, tag) of the batch followed by ingress (verify, decrypt,
@@ -64,7 +64,7 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=8.0, help="bounded CPU baseline sample length")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--prefix-pages", type=int, default=4096,
-                    help="BASELINE config 4: pages of the full-prefix sweep, split over the ranks (0 = skip)")
+                    help="pages of the full-prefix sweep (benchmark config 4), split over the ranks (0 = skip)")
     ap.add_argument("--prefix-chunk", type=int, default=256, help="pages per launch in the prefix sweep")
     ap.add_argument("--prefix-reps", type=int, default=3)
     return ap.parse_args()
@@ -439,7 +439,7 @@ def ours(args):
     if not torch.equal(host[0]["kout"], sets[0]["kout"].cpu()):
         raise RuntimeError("end-to-end output differs from the device-resident run")
 
-    # a 4,096-page prefix (64 layers x 64 pages) addressed through a seeded shuffled
+    # benchmark config 4: a 4,096-page prefix (64 layers x 64 pages) addressed through a seeded shuffled
     # block-table list, split into contiguous shards over the ranks (strong scaling).  Each rank holds only
     # its own blocks; egress of the whole shard, then ingress, for INT4_SYM and K8V4_ASYM, in chunks of
     # --prefix-chunk pages over the streams.

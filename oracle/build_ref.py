@@ -26,7 +26,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.environ.get("ZTCP_REF_BUILD_DIR", os.path.join(HERE, "_ref"))
 MODULE_NAME = "ztcp_ref_codec"
 REL_SOURCE = os.path.join("research", "baseline_codec", "csrc", "fused_cold_page_cpu.cpp")
-DEFAULT_ROOT = os.environ.get("ZTCP_REFERENCE_ROOT", "/root/reference")
+DEFAULT_ROOT = os.environ.get("ZTCP_REFERENCE_ROOT",
+                              os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference"))
 
 
 def built_module_path() -> str | None:

@@ -201,7 +201,8 @@ def make_digests(ref, torch):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-root", default=os.environ.get("ZTCP_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference-root", default=os.environ.get(
+        "ZTCP_REFERENCE_ROOT", os.path.join(os.path.dirname(REPO), "reference")))
     args = ap.parse_args()
     import torch
 

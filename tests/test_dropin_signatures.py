@@ -10,7 +10,9 @@ import sys
 import pytest
 import torch
 
-REF_ROOT = os.environ.get("ZTCP_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("ZTCP_REFERENCE_ROOT",
+                          os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                                       "reference"))
 
 
 class _Recorder:

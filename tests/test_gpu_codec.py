@@ -102,7 +102,7 @@ def test_full_size_digests_bf16_input(ext, case):
 
 
 def test_config0_256_pages_bit_exact(ext, oracle):
-    """BASELINE config 0 at full size: 256 GQA pages, INT4_SYM + PRESERVE_FP8, bf16 input."""
+    """Benchmark config 0 at full size: 256 GQA pages, INT4_SYM + PRESERVE_FP8, bf16 input."""
     from ztcp_b200 import workload
 
     k32, v32 = workload.kv_pages_np(256, workload.GQA, seed=42)

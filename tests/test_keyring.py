@@ -16,7 +16,9 @@ from ztcp_b200 import errors, ledger
 from ztcp_b200.keyring import SessionKeyRing
 
 PEPPER = b"p" * 32
-REF_ROOT = os.environ.get("ZTCP_REFERENCE_ROOT", "/root/reference")
+REF_ROOT = os.environ.get("ZTCP_REFERENCE_ROOT",
+                          os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                                       "reference"))
 
 
 @pytest.fixture(scope="module", autouse=True)
