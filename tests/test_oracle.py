@@ -180,7 +180,8 @@ def test_neon_mode_matches_numpy_restatement(oracle, preset):
         x = (rng.standard_normal((2, 16)) * scale_mag).astype(np.float32)
         if trial % 3 == 0:
             x.flat[rng.integers(0, 32, 3)] = rng.choice(edge, 3)
-        x16 = x.astype(np.float16)
+        with np.errstate(over="ignore"):  # magnitudes beyond 65504 become inf on purpose
+            x16 = x.astype(np.float16)
         k = x16[0].reshape(1, 1, 1, 16)
         v = x16[1].reshape(1, 1, 1, 16)
         exp = oracle.spec_payload_bytes(preset, 0, 1, 16, 0, True)

@@ -58,9 +58,9 @@ def _rank_main(rank, world, port, out):
 
 def test_two_gloo_ranks():
     world = 2
-    with mp.Manager() as mgr:
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
         out = mgr.dict()
-        ctx = mp.get_context("spawn")
         port = _free_port()
         procs = [ctx.Process(target=_rank_main, args=(r, world, port, out)) for r in range(world)]
         for p in procs:
