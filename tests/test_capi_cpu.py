@@ -75,6 +75,7 @@ def _encode(lib, **kw):
     b = capi.PageBatch()
     b.n_pages = a["n"]
     b.token_hash = a["token"]
+    b.options = a.get("options", 0)
     keys = capi.keys(1, 2, 3, 4, 5, 6)
     rc = lib.ztcp_encode_pages(a["k"], a["v"], a["dtype"], C.byref(a["geom"]), C.byref(b), a["preset"],
                                a["rope_mode"], a["exp"], C.byref(keys), a["out"], None)
@@ -94,6 +95,8 @@ def _encode(lib, **kw):
     (dict(token=None), "page_token_hashes must not be NULL"),
     (dict(k=FAKE + 8), "k_pages / v_pages must be 16-byte aligned"),
     (dict(dtype=7), "k_pages must be float16 or bfloat16"),
+    (dict(options=4), "unknown page batch options"),
+    (dict(options=capi.OPT_NEON_ARITH | 8), "unknown page batch options"),
 ])
 def test_encode_validation(lib, kw, msg):
     rc, err = _encode(lib, **kw)
@@ -126,3 +129,14 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
     monkeypatch.setattr(capi, "library_path", lambda: str(tmp_path / "absent.so"))
     with pytest.raises(ImportError, match="no CPU fallback"):
         capi.load()
+
+
+def test_decode_rejects_unknown_options(lib):
+    b = capi.PageBatch()
+    b.n_pages = 2
+    b.token_hash = FAKE
+    b.options = capi.OPT_PAGE_FALLBACK | 16
+    keys = capi.keys(1, 2, 3, 4, 5, 6)
+    g = capi.geometry(64, 8, 128, 64, False)
+    rc = lib.ztcp_decode_pages(FAKE, 98352, C.byref(g), C.byref(b), C.byref(keys), FAKE, FAKE, FAKE, FAKE, None)
+    assert rc == capi.ZTCP_EINVAL and lib.ztcp_last_error() == b"unknown page batch options"
