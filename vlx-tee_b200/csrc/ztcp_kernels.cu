@@ -17,6 +17,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <mutex>
 
 #include "ztcp_device.cuh"
 #include "ztcp_kernels.cuh"
@@ -630,9 +631,32 @@ __global__ void siphash_kernel(const uint8_t* src, int64_t len, uint64_t k0, uin
 // Shared memory a chain CTA takes: the sm_100 per-CTA maximum (227 KB), so it owns its SM.
 constexpr int kMacReserveBytes = 227 * 1024;
 
+// Dynamic shared memory above 48 KB needs a per-kernel, per-device opt-in.  It is raised, never lowered (a
+// lower setting would fail the launches of larger tiles made before), and set only when a launch needs more
+// than the kernel was opened to on this device.
+struct OptIn {
+  const void* fn;
+  int dev;
+  int32_t bytes;
+};
+std::mutex g_optin_mu;
+OptIn g_optin[64];
+int g_optin_n = 0;
+
 template <typename K>
 void ensure_smem(K kernel, int32_t bytes) {
-  if (bytes > 48 * 1024) cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (bytes <= 48 * 1024) return;
+  const void* fn = reinterpret_cast<const void*>(kernel);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(g_optin_mu);
+  OptIn* rec = nullptr;
+  for (int i = 0; i < g_optin_n; ++i)
+    if (g_optin[i].fn == fn && g_optin[i].dev == dev) rec = &g_optin[i];
+  if (rec && rec->bytes >= bytes) return;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (rec) rec->bytes = bytes;
+  else if (g_optin_n < 64) g_optin[g_optin_n++] = OptIn{fn, dev, bytes};
 }
 
 }  // namespace
