@@ -385,26 +385,33 @@ __device__ __forceinline__ void siphash_bytes(SipState& st, const uint8_t* p, in
     st.v3 = xor64(st.v3, load_word_any(p));  // word 0
     // Chunk c is read from the ring a 16-byte pair at a time right before its words are absorbed (the
     // shared-memory loads hide under the previous word's rounds); its last word looks ahead into chunk
-    // c+1, which has landed too.  (Staging each chunk through two 8 x uint4 register buffers instead was
-    // measured 4.5 % slower: 100.2 vs 95.7 cycles/word.)
+    // c+1, which has landed too.  The loop body absorbs four words: the chain runs concurrently with the
+    // tile kernels of other batches, and its code footprint costs them instruction-fetch bandwidth.
+    // Measured in the 32-batch bench (same call): 4 words per pass 1,791-1,808 GB/s, 8 words 1,714-1,720,
+    // 16 words 1,644-1,680, 32 words 1,450-1,466, 2 words 1,764, 1 word 1,731-1,748 -- although the chain
+    // alone is fastest at 16 or 32 words (95.6 vs 99.9 cycles/word at 4).
 #pragma unroll 1
     for (int64_t c = 0; c < n_chunks; ++c) {
       ring_fill(ring, p, c + kRing - 1, n_chunks);
       cp_async_wait<kRing - 2>();  // chunks c and c+1 landed
       const uint4* w = slot(c);
       const W64 last = c + 1 < n_chunks ? W64{slot(c + 1)[0].x, slot(c + 1)[0].y} : after;
+#pragma unroll 1
+      for (int h = 0; h < 4; ++h) {  // four words per pass: a short loop body (see below)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint4 q = w[j];
-        st.absorb_pre(W64{q.x, q.y}, W64{q.z, q.w});
-        W64 nx;
-        if (j < 7) {
-          const uint4 r = w[j + 1];
-          nx = W64{r.x, r.y};
-        } else {
-          nx = last;
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = 2 * h + jj;
+          const uint4 q = w[j];
+          st.absorb_pre(W64{q.x, q.y}, W64{q.z, q.w});
+          W64 nx;
+          if (j < 7) {
+            const uint4 r = w[j + 1];
+            nx = W64{r.x, r.y};
+          } else {
+            nx = last;
+          }
+          st.absorb_pre(W64{q.z, q.w}, nx);
         }
-        st.absorb_pre(W64{q.z, q.w}, nx);
       }
     }
     cp_async_wait<0>();
