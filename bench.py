@@ -248,7 +248,7 @@ def reference_arm(args):
     per_step_ms = 2 * args.pages * PAGE_HOT_BYTES / (base["value"] * 1e9) * 1e3
     line = {"metric": METRIC, "value": base["value"], "unit": "GB/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(per_step_ms, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp16", "data": "synthetic",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u32+f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "pages_per_gpu": args.pages, "host_cores": base["cores"]},
             "cpu_baseline": base,
             "e2e": {"value": base["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -516,10 +516,13 @@ def ours(args):
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": round(total_ms / K, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16 in, int4/int8 + fp16 scales, fp16 out",
+            "scaling": "weak", "vs_baseline": None, "dtype": "u32+f32",
             "data": "synthetic (seeded N(0,1), x15 RoPE outlier channels)",
             "config": {"workload": WORKLOAD,
                        "pages_per_gpu": n, "batches_in_flight": D,
+                       "io": "bf16 K/V in; INT4/INT8 + fp16 scales on the wire; fp16 K/V out",
+                       "arithmetic": "32-bit integer ARX (ChaCha20, SipHash-2-4 in 32-bit halves), "
+                                     "fp32/fp16 quantization",
                        "parallelism": f"pages sharded, {world} GPU(s), no collective",
                        "l2": f"{n_sets} input sets, {n_sets * n * (PAGE_HOT_BYTES * 2 + BLOB_BYTES) / 1e9:.2f} GB "
                              f"working set > 126 MB L2"},
