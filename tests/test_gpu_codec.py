@@ -524,3 +524,50 @@ def test_round_trip_replays_from_a_cuda_graph(ext, oracle):
         np.testing.assert_array_equal(ko.cpu().numpy().view(np.uint16), okd)
         np.testing.assert_array_equal(vo.cpu().numpy().view(np.uint16), ovd)
     del g
+
+
+def test_seeded_random_sweep(ext, oracle):
+    """120 seeded random configurations -- geometry (tokens, heads, head_dim up to 576, RoPE width), preset,
+    RoPE mode, GQA or single-buffer MLA, fp16 or bf16 input, page count, payload padding (so blob strides
+    of every alignment) and magnitudes from 1e-6 to 1e4 with edge values -- each encoded and decoded on the
+    GPU and compared byte for byte with the oracle."""
+    from ztcp_b200 import capi, codec, workload
+
+    rng = np.random.default_rng(20261202)
+    edge = np.array([np.inf, -np.inf, 65504, -65504, 1e-7, -3e-6, 0.0, 7e4], dtype=np.float32)
+    for case in range(120):
+        D = int(rng.choice([16, 32, 48, 64, 96, 128, 192, 256, 576]))
+        T, H = int(rng.integers(1, 65)), int(rng.integers(1, 9 if D <= 128 else 3))
+        rope = int(rng.integers(0, D // 16 + 1)) * 16
+        rope_mode = int(rng.integers(0, 3)) if rope > 0 else 0
+        preset, mla = int(rng.integers(1, 4)), bool(rng.random() < 0.3)
+        bf16, n, extra = bool(rng.random() < 0.5), int(rng.integers(1, 5)), int(rng.integers(0, 41))
+        x = (rng.standard_normal((2, n, T, H, D)) * 10.0 ** rng.uniform(-6, 4)).astype(np.float32)
+        mask = rng.random(x.shape) < 0.02
+        x[mask] = rng.choice(edge, int(mask.sum()))
+        with np.errstate(over="ignore"):
+            if bf16:
+                kt = torch.from_numpy(x[0]).to(torch.bfloat16)
+                vt = None if mla else torch.from_numpy(x[1]).to(torch.bfloat16)
+                k16, v16 = kt.half().numpy(), None if mla else vt.half().numpy()
+            else:
+                k16, v16 = x[0].astype(np.float16), None if mla else x[1].astype(np.float16)
+                kt, vt = torch.from_numpy(k16), None if mla else torch.from_numpy(v16)
+        m = workload.session_material(int(rng.integers(1 << 30)))
+        toks = workload.token_hashes(n, int(rng.integers(1 << 30)))
+        exp = oracle.spec_payload_bytes(preset, rope_mode, T * H, D, rope, not mla) + extra
+        keys = capi.keys(*m["key"], *m["mac_key"])
+        tag = f"case {case}: T{T} H{H} D{D} rope{rope} preset{preset} mode{rope_mode} mla{mla} bf16{bf16} n{n} +{extra}"
+        blobs = torch.empty((n, 48 + exp), dtype=torch.uint8, device=DEV)
+        codec.encode_pages(kt.to(DEV), None if vt is None else vt.to(DEV), torch.from_numpy(toks.view(np.int64)).to(DEV),
+                           blobs, rope_dim=rope, preset=preset, rope_mode=rope_mode, expected_payload_bytes=exp,
+                           tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"],
+                           head_group_id=m["head_group"], base_sequence_nonce=m["base_seq"], keys=keys)
+        want = helpers.oracle_encode(oracle, k16, v16, toks, rope, preset, rope_mode, exp, m)
+        np.testing.assert_array_equal(blobs.cpu().numpy(), want, err_msg=tag)
+        kd, vd = gpu_decode(ext, blobs, torch.from_numpy(toks.view(np.int64)), k16.shape, rope, mla, m)
+        okd, ovd, _, first = helpers.oracle_decode(oracle, want, toks, k16.shape, rope, mla, m)
+        assert first == -1, tag
+        np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd, err_msg=tag)
+        if not mla:
+            np.testing.assert_array_equal(vd.cpu().numpy().view(np.uint16), ovd, err_msg=tag)
