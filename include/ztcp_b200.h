@@ -122,7 +122,8 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
  * against `batch`, the SipHash tag, then flags and length; writes status[i] (device int32,
  * ZTCP_PAGE_*) and sets *any_fail (device int32, zeroed by this call) when any page fails.  Only
  * then decrypts and dequantizes into out_k / out_v (device fp16, page i at kv_block[i]); when any
- * page of the batch failed, every output page of the batch is zeroed instead (csrc:2481-2495).
+ * page of the batch failed, every output page of the batch is zeroed instead (csrc:2481-2495) -- or,
+ * with ZTCP_OPT_PAGE_FALLBACK in batch->options, only the failed pages.
  * out_v must be NULL for a single-buffer MLA geometry and non-NULL otherwise.
  * Replaces fused_decode_cold_pages_peak_into_cpu (csrc:2250-2496) and, with n_pages = 1,
  * fused_decode_cold_page_cpu (csrc:1557-1773). */
