@@ -156,6 +156,29 @@ int32_t ztcp_siphash24_128(const uint8_t* src, int64_t len, uint64_t mk0, uint64
 int32_t ztcp_gather(uint8_t* dst, int32_t dst_device, const uint8_t* const* srcs, const int32_t* src_devices,
                     const int64_t* bytes, int32_t n, void* stream);
 
+/* Largest batch ztcp_decode_pages_noalloc takes in one call. */
+#define ZTCP_NOALLOC_MAX_PAGES 65536
+
+/* Ingress that needs no device memory from the caller beyond its inputs, its K/V outputs and a one-word
+ * any_fail flag -- an addition of this library with no counterpart in the reference.  ztcp_decode_pages
+ * asks for a per-page status array (the tag check's verdicts, read by the decrypt pass); this variant
+ * keeps those verdicts in a buffer inside the library, so it suits callers that cannot call cudaMalloc on
+ * the decode path: a serving engine that hands all device memory to its KV pool at start-up and allows no
+ * allocation while requests run (one could fail or stall on a full device), or a plugin loaded into such
+ * an engine that only sees the engine's buffers.  Otherwise it behaves as ztcp_decode_pages: same checks,
+ * same outputs, *any_fail (device int32) zeroed by the call and set when a page fails, every output page
+ * zeroed then (only the failed ones with ZTCP_OPT_PAGE_FALLBACK); per-page statuses are not returned.
+ * Limits: at most ZTCP_NOALLOC_MAX_PAGES pages per call (larger batches return ZTCP_EINVAL; split them);
+ * the buffer (ZTCP_NOALLOC_MAX_PAGES x 4 bytes = 256 KiB) stays on every GPU that loads the library
+ * until the process exits.  All calls on a device share that one buffer and each overwrites it, so calls
+ * that overlap on the GPU (streams not ordered against each other) race and can decode or zero the wrong
+ * pages: issue them on one stream or order them with events.  The first call on each device looks up the
+ * buffer's address there (a one-time set-up, done with that device current); make that first call before
+ * any stream capture. */
+int32_t ztcp_decode_pages_noalloc(const uint8_t* blobs, int64_t blob_bytes, const ztcp_geometry* geom,
+                                  const ztcp_page_batch* batch, const ztcp_keys* keys, uint16_t* out_k,
+                                  uint16_t* out_v, int32_t* any_fail, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

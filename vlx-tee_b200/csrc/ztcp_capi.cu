@@ -7,6 +7,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <mutex>
 #include <string>
 
 #include "../../include/ztcp_b200.h"
@@ -314,3 +315,62 @@ int32_t ztcp_gather(uint8_t* dst, int32_t dst_device, const uint8_t* const* srcs
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------
+// Decode for callers that cannot allocate device memory (no counterpart in the reference)
+// ------------------------------------------------------------------------------------------------
+// ztcp_decode_pages takes from its caller the per-page status array through which the tag-check kernel
+// tells the decrypt kernel which pages failed.  ztcp_decode_pages_noalloc keeps that array here instead:
+// one per GPU, ZTCP_NOALLOC_MAX_PAGES entries (256 KiB), resident on every GPU that loads this library
+// until the process exits.  Host code may not use the array's name as a device address; its address on
+// each device is looked up once, with that device current, and handed to the unchanged decode path.
+static __device__ __align__(256) int32_t g_noalloc_status[ZTCP_NOALLOC_MAX_PAGES];
+
+namespace {
+
+constexpr int kNoallocDevices = 64;
+std::mutex g_noalloc_mu;
+int32_t* g_noalloc_addr[kNoallocDevices];  // g_noalloc_status on device i, once looked up
+
+int32_t noalloc_status_array(int32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(ZTCP_ECUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (dev >= 0 && dev < kNoallocDevices && g_noalloc_addr[dev]) {
+    *out = g_noalloc_addr[dev];
+    return ZTCP_OK;
+  }
+  int32_t* ptr = nullptr;
+  e = cudaGetSymbolAddress((void**)&ptr, g_noalloc_status);
+  if (e != cudaSuccess || ptr == nullptr)
+    return fail(ZTCP_ECUDA, std::string("cudaGetSymbolAddress of the no-allocation status array: ") +
+                                cudaGetErrorString(e));
+  if (dev >= 0 && dev < kNoallocDevices) g_noalloc_addr[dev] = ptr;
+  *out = ptr;
+  return ZTCP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t ztcp_decode_pages_noalloc(const uint8_t* blobs, int64_t blob_bytes, const ztcp_geometry* geom,
+                                  const ztcp_page_batch* batch, const ztcp_keys* keys, uint16_t* out_k,
+                                  uint16_t* out_v, int32_t* any_fail, void* stream) {
+  if (!batch) return fail(ZTCP_EINVAL, "page batch must not be NULL");
+  if (batch->n_pages > ZTCP_NOALLOC_MAX_PAGES)
+    return fail(ZTCP_EINVAL, "batch of " + std::to_string(batch->n_pages) +
+                                 " pages exceeds the no-allocation decode's limit of " +
+                                 std::to_string(ZTCP_NOALLOC_MAX_PAGES) + " pages per call");
+  if (!any_fail) return fail(ZTCP_EINVAL, "any_fail must not be NULL");
+  int32_t* status = nullptr;
+  const int32_t rc = noalloc_status_array(&status);
+  if (rc != ZTCP_OK) return rc;
+  // every page's status is written by the tag check before the decrypt pass reads it, and any_fail is
+  // zeroed by the decode itself, so nothing left over from an earlier call is read
+  return ztcp_decode_pages(blobs, blob_bytes, geom, batch, keys, out_k, out_v, status, any_fail, stream);
+}
+
+}  // extern "C"
+

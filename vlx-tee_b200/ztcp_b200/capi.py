@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "ztcp_chacha20_xor",
     "ztcp_siphash24_128",
     "ztcp_gather",
+    "ztcp_decode_pages_noalloc",
 )
 
 
@@ -71,6 +72,7 @@ class PageBatch(C.Structure):
 
 OPT_NEON_ARITH = 1
 OPT_PAGE_FALLBACK = 2
+NOALLOC_MAX_PAGES = 65536  # ZTCP_NOALLOC_MAX_PAGES
 
 
 class ZtcpError(RuntimeError):
@@ -117,6 +119,9 @@ def load() -> C.CDLL:
     L.ztcp_chacha20_xor.argtypes = [vp, vp, i64, C.c_char_p, u32, C.c_char_p, vp]
     L.ztcp_siphash24_128.restype = i32
     L.ztcp_siphash24_128.argtypes = [vp, i64, u64, u64, vp, vp]
+    L.ztcp_decode_pages_noalloc.restype = i32
+    L.ztcp_decode_pages_noalloc.argtypes = [vp, i64, C.POINTER(Geometry), C.POINTER(PageBatch), C.POINTER(Keys), vp,
+                                            vp, vp, vp]
     L.ztcp_gather.restype = i32
     L.ztcp_gather.argtypes = [vp, i32, C.POINTER(vp), C.POINTER(i32), C.POINTER(i64), i32, vp]
     _lib = L
