@@ -571,3 +571,52 @@ def test_seeded_random_sweep(ext, oracle):
         np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd, err_msg=tag)
         if not mla:
             np.testing.assert_array_equal(vd.cpu().numpy().view(np.uint16), ovd, err_msg=tag)
+
+
+def test_neon_option_random_sweep(ext, oracle):
+    """The NEON-arithmetic egress option on 40 seeded random configurations (geometry, preset, RoPE mode,
+    GQA/MLA, fp16/bf16, padding, magnitudes 1e-6 to 1e4 with edge values): bytes equal the oracle's NEON
+    restatement and the blobs decode to the oracle's pages."""
+    from ztcp_b200 import capi, codec, workload
+
+    rng = np.random.default_rng(4242)
+    edge = np.array([np.inf, -np.inf, 65504, -65504, 1e-7, -3e-6, 0.0, 7e4], dtype=np.float32)
+    for case in range(40):
+        D = int(rng.choice([16, 32, 64, 96, 128, 192, 576]))
+        T, H = int(rng.integers(1, 49)), int(rng.integers(1, 9 if D <= 128 else 3))
+        rope = int(rng.integers(0, D // 16 + 1)) * 16
+        rope_mode = int(rng.integers(0, 3)) if rope > 0 else 0
+        preset, mla = int(rng.integers(1, 4)), bool(rng.random() < 0.3)
+        bf16, n, extra = bool(rng.random() < 0.5), int(rng.integers(1, 4)), int(rng.integers(0, 33))
+        x = (rng.standard_normal((2, n, T, H, D)) * 10.0 ** rng.uniform(-6, 4)).astype(np.float32)
+        mask = rng.random(x.shape) < 0.02
+        x[mask] = rng.choice(edge, int(mask.sum()))
+        with np.errstate(over="ignore"):
+            if bf16:
+                kt = torch.from_numpy(x[0]).to(torch.bfloat16)
+                vt = None if mla else torch.from_numpy(x[1]).to(torch.bfloat16)
+                k16, v16 = kt.half().numpy(), None if mla else vt.half().numpy()
+            else:
+                k16, v16 = x[0].astype(np.float16), None if mla else x[1].astype(np.float16)
+                kt, vt = torch.from_numpy(k16), None if mla else torch.from_numpy(v16)
+        m = workload.session_material(int(rng.integers(1 << 30)))
+        toks = workload.token_hashes(n, int(rng.integers(1 << 30)))
+        exp = oracle.spec_payload_bytes(preset, rope_mode, T * H, D, rope, not mla) + extra
+        tag = f"case {case}: T{T} H{H} D{D} rope{rope} preset{preset} mode{rope_mode} mla{mla} bf16{bf16} n{n} +{extra}"
+        blobs = torch.empty((n, 48 + exp), dtype=torch.uint8, device=DEV)
+        codec.encode_pages(kt.to(DEV), None if vt is None else vt.to(DEV), torch.from_numpy(toks.view(np.int64)).to(DEV),
+                           blobs, rope_dim=rope, preset=preset, rope_mode=rope_mode, expected_payload_bytes=exp,
+                           tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"],
+                           head_group_id=m["head_group"], base_sequence_nonce=m["base_seq"],
+                           keys=capi.keys(*m["key"], *m["mac_key"]), neon_arith=True)
+        want = oracle.encode_batch(k16.view(np.uint16), None if v16 is None else v16.view(np.uint16), toks,
+                                   rope_dim=rope, preset=preset, rope_mode=rope_mode, expected_payload=exp,
+                                   tenant=m["tenant"], model=m["model"], layer=m["layer"], head_group=m["head_group"],
+                                   base_seq=m["base_seq"], key=m["key"], mac_key=m["mac_key"], neon=True)
+        np.testing.assert_array_equal(blobs.cpu().numpy(), want, err_msg=tag)
+        kd, vd = gpu_decode(ext, blobs, torch.from_numpy(toks.view(np.int64)), k16.shape, rope, mla, m)
+        okd, ovd, _, first = helpers.oracle_decode(oracle, want, toks, k16.shape, rope, mla, m)
+        assert first == -1, tag
+        np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd, err_msg=tag)
+        if not mla:
+            np.testing.assert_array_equal(vd.cpu().numpy().view(np.uint16), ovd, err_msg=tag)

@@ -118,3 +118,57 @@ def test_hook_store_load_and_per_page_misses(hook):
     hc.ring.release(view)
     hc.ring.release(view2)
     assert hc.ring.free_slots == 32
+
+
+def test_page_fallback_random_sweep(oracle):
+    """Per-page fallback decode on 30 seeded random configurations with random pages tampered (ciphertext
+    bit, tenant byte of the header, magic): statuses equal the oracle's, every untampered page equals the
+    oracle's decode of the untouched blobs, every tampered page is zero, and the batch flag is set."""
+    from ztcp_b200 import build, capi, codec, workload
+
+    build.build()
+    rng = np.random.default_rng(777)
+    for case in range(30):
+        D = int(rng.choice([16, 48, 64, 128, 576]))
+        T, H = int(rng.integers(1, 33)), int(rng.integers(1, 9 if D <= 128 else 2))
+        rope = int(rng.integers(0, D // 16 + 1)) * 16
+        rope_mode = int(rng.integers(0, 3)) if rope > 0 else 0
+        preset, mla, n = int(rng.integers(1, 4)), bool(rng.random() < 0.3), int(rng.integers(2, 7))
+        k16 = rng.standard_normal((n, T, H, D)).astype(np.float16)
+        v16 = None if mla else rng.standard_normal((n, T, H, D)).astype(np.float16)
+        m = workload.session_material(int(rng.integers(1 << 30)))
+        toks = workload.token_hashes(n, int(rng.integers(1 << 30)))
+        exp = oracle.spec_payload_bytes(preset, rope_mode, T * H, D, rope, not mla)
+        clean = helpers.oracle_encode(oracle, k16, v16, toks, rope, preset, rope_mode, exp, m)
+        okd, ovd, _, first = helpers.oracle_decode(oracle, clean, toks, k16.shape, rope, mla, m)
+        assert first == -1
+        bad = clean.copy()
+        tampered = rng.choice(n, int(rng.integers(1, n)), replace=False)
+        for i in tampered:
+            kind = int(rng.integers(0, 3))
+            if kind == 0:
+                bad[i, 32 + int(rng.integers(0, exp))] ^= 1 << int(rng.integers(0, 8))  # ciphertext
+            elif kind == 1:
+                bad[i, 4] ^= 0x01  # tenant hash
+            else:
+                bad[i, 0] ^= 0x01  # magic
+        _, _, ost, _ = helpers.oracle_decode(oracle, bad, toks, k16.shape, rope, mla, m)
+        ko = torch.full(k16.shape, 3.0, dtype=torch.float16, device=DEV)
+        vo = None if mla else torch.full(k16.shape, 3.0, dtype=torch.float16, device=DEV)
+        status, fail = codec.decode_pages(torch.from_numpy(bad).to(DEV), torch.from_numpy(toks.view(np.int64)).to(DEV),
+                                          ko, vo, rope_dim=rope, is_mla=mla, tenant_id_hash=m["tenant"],
+                                          model_id_hash=m["model"], layer_id=m["layer"],
+                                          keys=capi.keys(*m["key"], *m["mac_key"]), page_fallback=True)
+        tag = f"case {case}: T{T} H{H} D{D} rope{rope} preset{preset} mode{rope_mode} mla{mla} n{n} bad{sorted(tampered)}"
+        st = status.cpu().numpy()
+        np.testing.assert_array_equal(st, np.asarray(ost), err_msg=tag)
+        assert int(fail.item()) == 1, tag
+        kh = ko.cpu().numpy().view(np.uint16)
+        vh = None if mla else vo.cpu().numpy().view(np.uint16)
+        for i in range(n):
+            if st[i] == 0:
+                np.testing.assert_array_equal(kh[i], okd[i], err_msg=tag)
+                if not mla:
+                    np.testing.assert_array_equal(vh[i], ovd[i], err_msg=tag)
+            else:
+                assert not kh[i].any() and (mla or not vh[i].any()), tag
