@@ -40,3 +40,23 @@ def test_reference_arm_line():
 def test_reference_arm_falls_back_to_the_oracle(tmp_path):
     d = _run({"ZTCP_REF_BUILD_DIR": str(tmp_path)})  # an empty build directory: no reference module
     assert d["cpu_baseline"]["kind"] == "port" and d["value"] > 0
+
+
+def test_reference_arm_under_torchrun_prints_once():
+    """Launched like the driver's multi-GPU runs (torchrun, two ranks): rank 0 alone runs the reference codec
+    and prints its line; the other rank exits 0 without work."""
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    out = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
+                          "--master-addr", "127.0.0.1", "--master-port", str(port),
+                          os.path.join(REPO, "bench.py"), "--impl", "reference", "--gpus", "2", "--steps", "3",
+                          "--warmup", "3", "--cpu-seconds", "0.5"], capture_output=True, text=True, timeout=300,
+                         cwd=REPO)
+    assert out.returncode == 0, out.stderr[-2000:]
+    lines = [l for l in out.stdout.splitlines() if l.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference" and d["n_gpus"] == 2 and d["value"] > 0
