@@ -140,3 +140,21 @@ def test_decode_rejects_unknown_options(lib):
     g = capi.geometry(64, 8, 128, 64, False)
     rc = lib.ztcp_decode_pages(FAKE, 98352, C.byref(g), C.byref(b), C.byref(keys), FAKE, FAKE, FAKE, FAKE, None)
     assert rc == capi.ZTCP_EINVAL and lib.ztcp_last_error() == b"unknown page batch options"
+
+
+def test_noalloc_decode_validation(lib):
+    """The no-allocation decode rejects a missing batch, a missing fail flag and batches beyond its fixed
+    buffer before it touches a GPU."""
+    keys = capi.keys(1, 2, 3, 4, 5, 6)
+    g = capi.geometry(64, 8, 128, 64, False)
+    rc = lib.ztcp_decode_pages_noalloc(FAKE, 98352, C.byref(g), None, C.byref(keys), FAKE, FAKE, FAKE, None)
+    assert rc == capi.ZTCP_EINVAL and lib.ztcp_last_error() == b"page batch must not be NULL"
+    b = capi.PageBatch()
+    b.n_pages = 2
+    b.token_hash = FAKE
+    rc = lib.ztcp_decode_pages_noalloc(FAKE, 98352, C.byref(g), C.byref(b), C.byref(keys), FAKE, FAKE, None, None)
+    assert rc == capi.ZTCP_EINVAL and lib.ztcp_last_error() == b"any_fail must not be NULL"
+    b.n_pages = capi.NOALLOC_MAX_PAGES + 1
+    rc = lib.ztcp_decode_pages_noalloc(FAKE, 98352, C.byref(g), C.byref(b), C.byref(keys), FAKE, FAKE, FAKE, None)
+    assert rc == capi.ZTCP_EINVAL
+    assert lib.ztcp_last_error() == b"batch of 65537 pages exceeds the no-allocation decode's limit of 65536 pages per call"
