@@ -45,6 +45,8 @@ extern "C" {
 #define ZTCP_PAGE_MAC_FAILED 3     /* SipHash-2-4-128 tag mismatch */
 #define ZTCP_PAGE_BAD_FLAGS 4      /* preset or rope_mode out of range */
 #define ZTCP_PAGE_TRUNCATED 5      /* payload shorter than the flags require */
+#define ZTCP_PAGE_BAD_BLOCK 6      /* kv_block[i] outside [0, kv_pool_pages): the page is neither read nor written
+                                      (an extension: the reference's batch calls take contiguous pages) */
 
 /* KV page geometry: a page is num_tokens x num_heads x head_dim elements per buffer. */
 typedef struct ztcp_geometry {
@@ -69,7 +71,12 @@ typedef struct ztcp_keys {
  *   seq nonce    sequence_nonce[i]  (device uint64; NULL = base_sequence_nonce + i, csrc:1994)
  *   layer id     layer_id[i]        (device uint16; NULL = layer_id_uniform)
  * tenant / model hash and head group are shared by the batch.  For decode these are the EXPECTED
- * values the header must carry.  kv_block entries must lie in [0, pages in the KV pool).
+ * values the header must carry.
+ * kv_pool_pages: pages in the KV pool(s) the batch addresses.  Required (> 0) with a block table: the
+ * kernels check every kv_block entry against it before any access, on the device.  A page whose entry
+ * lies outside [0, kv_pool_pages) is never read or written in the pool: encode writes that page's blob
+ * as all-zero bytes (magic 0, which every decode rejects), decode reports ZTCP_PAGE_BAD_BLOCK for it
+ * and sets *any_fail.  Without a block table, 0 means "not given"; a positive value must be >= n_pages.
  * options: ZTCP_OPT_* bits (0 = the reference's scalar x86-64 arithmetic, bit-exact with its build). */
 #define ZTCP_OPT_NEON_ARITH 1 /* egress: quantize with the reference's ARM NEON fp16 arithmetic (its build with
                                  __ARM_FEATURE_FP16_VECTOR_ARITHMETIC, csrc:718-733 / :786-803); decode ignores it */
@@ -90,6 +97,7 @@ typedef struct ztcp_page_batch {
   uint16_t layer_id_uniform;
   uint16_t head_group_id;
   int32_t options;
+  int64_t kv_pool_pages;
 } ztcp_page_batch;
 
 /* Message of the last failed call on this thread ("" when none). */
@@ -174,7 +182,8 @@ int32_t ztcp_gather(uint8_t* dst, int32_t dst_device, const uint8_t* const* srcs
  * that overlap on the GPU (streams not ordered against each other) race and can decode or zero the wrong
  * pages: issue them on one stream or order them with events.  The first call on each device looks up the
  * buffer's address there (a one-time set-up, done with that device current); make that first call before
- * any stream capture. */
+ * any stream capture.  The address is kept for the life of the process, so resetting a device
+ * (cudaDeviceReset) after its first call is not supported: the library's device memory may move. */
 int32_t ztcp_decode_pages_noalloc(const uint8_t* blobs, int64_t blob_bytes, const ztcp_geometry* geom,
                                   const ztcp_page_batch* batch, const ztcp_keys* keys, uint16_t* out_k,
                                   uint16_t* out_v, int32_t* any_fail, void* stream);

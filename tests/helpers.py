@@ -59,19 +59,7 @@ def oracle_decode(oracle, blobs, toks, shape4, rope_dim, mla, m):
 
 
 def attention_output_cosine(k_ref, v_ref, k_hat, v_hat, n_queries: int = 32, seed: int = 99) -> float:
-    """Simulated single-page attention fidelity (reference bench:97-146, with `n_queries` queries per head):
-    attention-output cosine when V is present, softmax-weights cosine otherwise; float64."""
-    import torch
+    """The reference benchmark's fidelity metric (bench:97-146); see ztcp_b200.workload.attention_cosine."""
+    from ztcp_b200 import workload
 
-    g = torch.Generator().manual_seed(seed)
-    kr, kh = k_ref.double(), k_hat.double()
-    T, H, D = kr.shape[-3:]
-    q = torch.randn((n_queries, H, D), generator=g, dtype=torch.float64)
-    scale = D ** -0.5
-    a_ref = torch.softmax(torch.einsum("qhd,...thd->...qht", q, kr) * scale, dim=-1)
-    a_hat = torch.softmax(torch.einsum("qhd,...thd->...qht", q, kh) * scale, dim=-1)
-    if v_ref is not None:
-        o_ref = torch.einsum("...qht,...thd->...qhd", a_ref, v_ref.double())
-        o_hat = torch.einsum("...qht,...thd->...qhd", a_hat, v_hat.double())
-        return float(torch.nn.functional.cosine_similarity(o_ref.reshape(-1), o_hat.reshape(-1), dim=0))
-    return float(torch.nn.functional.cosine_similarity(a_ref.reshape(-1), a_hat.reshape(-1), dim=0))
+    return workload.attention_cosine(k_ref, v_ref, k_hat, v_hat, n_queries=n_queries, seed=seed)

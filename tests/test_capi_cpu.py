@@ -14,6 +14,7 @@ from ztcp_b200.cold_page_spec import ColdPageAAD, ColdPageGeometry, QuantPreset,
 INCLUDE = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
 HEADER = os.path.join(INCLUDE, "ztcp_b200.h")
 LEDGER_HEADER = os.path.join(INCLUDE, "ztcp_ledger.h")
+MEASURE_HEADER = os.path.join(INCLUDE, "ztcp_measure.h")
 
 
 @pytest.fixture(scope="module")
@@ -34,7 +35,9 @@ def test_exports_every_declared_symbol(lib):
     assert set(names) == set(capi.EXPORTED_SYMBOLS)
     ledger_names = declared_functions(LEDGER_HEADER)
     assert set(ledger_names) == set(ledger.LEDGER_SYMBOLS)
-    for n in names + ledger_names:
+    measure_names = declared_functions(MEASURE_HEADER)
+    assert set(measure_names) == set(capi.MEASURE_SYMBOLS)
+    for n in names + ledger_names + measure_names:
         assert hasattr(lib, n), n
     assert lib.ztcp_version() >= 100
 
@@ -158,3 +161,33 @@ def test_noalloc_decode_validation(lib):
     rc = lib.ztcp_decode_pages_noalloc(FAKE, 98352, C.byref(g), C.byref(b), C.byref(keys), FAKE, FAKE, FAKE, None)
     assert rc == capi.ZTCP_EINVAL
     assert lib.ztcp_last_error() == b"batch of 65537 pages exceeds the no-allocation decode's limit of 65536 pages per call"
+
+
+def test_pool_size_validation(lib):
+    """A block table needs the pool size its entries are checked against on the device; without a table a
+    given pool size must hold the batch."""
+    keys = capi.keys(1, 2, 3, 4, 5, 6)
+    g = capi.geometry(64, 8, 128, 64, False)
+    b = capi.PageBatch()
+    b.n_pages = 4
+    b.token_hash = FAKE
+    b.kv_block = FAKE
+    rc = lib.ztcp_decode_pages(FAKE, 98352, C.byref(g), C.byref(b), C.byref(keys), FAKE, FAKE, FAKE, FAKE, None)
+    assert rc == capi.ZTCP_EINVAL and lib.ztcp_last_error().startswith(b"kv_pool_pages is required")
+    rc = lib.ztcp_encode_pages(FAKE, FAKE, 1, C.byref(g), C.byref(b), 1, 1, 98304, C.byref(keys), FAKE, None)
+    assert rc == capi.ZTCP_EINVAL and lib.ztcp_last_error().startswith(b"kv_pool_pages is required")
+    b.kv_pool_pages = -1
+    rc = lib.ztcp_verify_pages(FAKE, 98352, C.byref(g), C.byref(b), C.byref(keys), FAKE, FAKE, None)
+    assert rc == capi.ZTCP_EINVAL and lib.ztcp_last_error() == b"kv_pool_pages must be non-negative"
+    b.kv_block = None
+    b.kv_pool_pages = 3
+    rc = lib.ztcp_decode_pages(FAKE, 98352, C.byref(g), C.byref(b), C.byref(keys), FAKE, FAKE, FAKE, FAKE, None)
+    assert rc == capi.ZTCP_EINVAL and lib.ztcp_last_error() == b"batch has more pages than kv_pool_pages"
+
+
+def test_measurement_entry_points_validate(lib):
+    out = capi.IntPeaks()
+    assert lib.ztcp_measure_int_peaks(None, capi.MEASURE_SCRATCH_BYTES, C.byref(out)) == capi.ZTCP_EINVAL
+    assert lib.ztcp_last_error() == b"scratch and out must not be NULL"
+    assert lib.ztcp_measure_int_peaks(FAKE + 4, capi.MEASURE_SCRATCH_BYTES, C.byref(out)) == capi.ZTCP_EINVAL
+    assert lib.ztcp_mark_phase(None) == capi.ZTCP_OK

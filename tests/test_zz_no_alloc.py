@@ -35,7 +35,7 @@ def _batch(n, seed, tamper_page=None):
     return m, toks, keys, blobs
 
 
-def _decode_both(lib, m, toks, keys, blobs):
+def _decode_both(lib, m, toks, keys, blobs, page_fallback=False):
     from ztcp_b200 import capi, codec
 
     n = blobs.shape[0]
@@ -44,13 +44,14 @@ def _decode_both(lib, m, toks, keys, blobs):
     vo_ref = torch.full_like(ko_ref, 5.0)
     _, fail_ref = codec.decode_pages(blobs, toks, ko_ref, vo_ref, rope_dim=64, is_mla=False,
                                      tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"],
-                                     keys=keys)
+                                     keys=keys, page_fallback=page_fallback)
     # the no-allocation entry point through the C-ABI: only inputs, outputs and the fail flag
     ko = torch.full_like(ko_ref, 9.0)
     vo = torch.full_like(ko_ref, 9.0)
     fail = torch.full((1,), 7, dtype=torch.int32, device=DEV)
     geom = capi.geometry(64, 8, 128, 64, False)
-    batch = codec._page_batch(n, toks, None, None, None, 0, m["tenant"], m["model"], m["layer"], 0)
+    batch = codec._page_batch(n, toks, None, None, None, 0, m["tenant"], m["model"], m["layer"], 0,
+                              capi.OPT_PAGE_FALLBACK if page_fallback else 0)
     rc = lib.ztcp_decode_pages_noalloc(blobs.data_ptr(), blobs.shape[1], C.byref(geom), C.byref(batch),
                                        C.byref(keys), ko.data_ptr(), vo.data_ptr(), fail.data_ptr(),
                                        torch.cuda.current_stream(DEV).cuda_stream)
@@ -76,6 +77,28 @@ def test_noalloc_decode_equals_decode_pages_call_after_call():
         assert torch.equal(vo.view(torch.int16), vo_ref.view(torch.int16))
         if want_fail:
             assert not ko.any() and not vo.any()
+
+
+def test_noalloc_page_fallback_reads_this_calls_verdicts():
+    """With the per-page fallback the decrypt pass reads the library's status array page by page: a tampered
+    batch zeroes only its failing page, and a following clean batch of as many or fewer pages zeroes none --
+    no verdict of one call leaks into the next."""
+    from ztcp_b200 import build, capi
+
+    build.build()
+    lib = capi.load()
+    tampered = _batch(6, 311, tamper_page=2)
+    clean_same = _batch(6, 312)
+    clean_fewer = _batch(4, 313)
+    for case, bad_page in ((tampered, 2), (clean_same, None), (clean_fewer, None), (tampered, 2)):
+        m, toks, keys, blobs = case
+        (ko_ref, vo_ref, f_ref), (ko, vo, f) = _decode_both(lib, m, toks, keys, blobs, page_fallback=True)
+        assert f_ref == f == (1 if bad_page is not None else 0)
+        assert torch.equal(ko.view(torch.int16), ko_ref.view(torch.int16))
+        assert torch.equal(vo.view(torch.int16), vo_ref.view(torch.int16))
+        for p in range(blobs.shape[0]):
+            zeroed = not ko[p].any() and not vo[p].any()
+            assert zeroed == (p == bad_page), p
 
 
 def test_noalloc_decode_rejects_batches_beyond_its_buffer():

@@ -49,12 +49,18 @@ int32_t check_batch(const ztcp_page_batch* b) {
   if (b->n_pages <= 0) return fail(ZTCP_EINVAL, "batch must hold at least one page");
   if (!b->token_hash) return fail(ZTCP_EINVAL, "page_token_hashes must not be NULL");
   if (b->options & ~(ZTCP_OPT_NEON_ARITH | ZTCP_OPT_PAGE_FALLBACK)) return fail(ZTCP_EINVAL, "unknown page batch options");
+  if (b->kv_pool_pages < 0) return fail(ZTCP_EINVAL, "kv_pool_pages must be non-negative");
+  if (b->kv_block && b->kv_pool_pages == 0)
+    return fail(ZTCP_EINVAL, "kv_pool_pages is required with a block table (kv_block entries are checked against it)");
+  if (!b->kv_block && b->kv_pool_pages > 0 && b->n_pages > b->kv_pool_pages)
+    return fail(ZTCP_EINVAL, "batch has more pages than kv_pool_pages");
   return ZTCP_OK;
 }
 
 ztcp::PageMeta to_meta(const ztcp_page_batch* b) {
   ztcp::PageMeta m;
   m.kv_block = b->kv_block;
+  m.pool_pages = b->kv_pool_pages;
   m.token_hash = b->token_hash;
   m.sequence_nonce = b->sequence_nonce;
   m.layer_id = b->layer_id;
@@ -88,6 +94,8 @@ int32_t launch_status(const char* what) {
 }
 
 }  // namespace
+
+int32_t ztcp::set_last_error(int32_t code, const std::string& msg) { return fail(code, msg); }
 
 extern "C" {
 
@@ -169,6 +177,8 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
   M.n_pages = batch->n_pages;
   M.mk0 = keys->mac[0];
   M.mk1 = keys->mac[1];
+  M.meta = P.meta;
+  ztcp::take_phase_mark(s);
   ztcp::launch_mac(M, false, s);
   return launch_status("mac_kernel<sign>");
 }
@@ -274,6 +284,7 @@ int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_g
 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = launch_verify(M, s)) != ZTCP_OK) return rc;
+  ztcp::take_phase_mark(s);
   ztcp::launch_ingress(P, s);
   return launch_status("ingress_tile_kernel");
 }
@@ -323,7 +334,9 @@ int32_t ztcp_gather(uint8_t* dst, int32_t dst_device, const uint8_t* const* srcs
 // tells the decrypt kernel which pages failed.  ztcp_decode_pages_noalloc keeps that array here instead:
 // one per GPU, ZTCP_NOALLOC_MAX_PAGES entries (256 KiB), resident on every GPU that loads this library
 // until the process exits.  Host code may not use the array's name as a device address; its address on
-// each device is looked up once, with that device current, and handed to the unchanged decode path.
+// each device is looked up once, with that device current, and handed to the unchanged decode path.  The
+// address is cached for the life of the process: after a cudaDeviceReset the module (and this array) could
+// be loaded elsewhere, so a reset after the first call on a device is documented as unsupported.
 static __device__ __align__(256) int32_t g_noalloc_status[ZTCP_NOALLOC_MAX_PAGES];
 
 namespace {

@@ -1,15 +1,20 @@
 // ztcp_kernels.cuh -- kernel parameter blocks shared by the kernels and the host launchers.
 #pragma once
+#include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <string>
 
 #include "ztcp_layout.h"
 
 namespace ztcp {
 
 // Per-page metadata of a batch.  Device pointers may be null: kv_block -> identity, sequence_nonce ->
-// seq_base + page index (the reference's batch rule, csrc:1994), layer_id -> layer_uniform.
+// seq_base + page index (the reference's batch rule, csrc:1994), layer_id -> layer_uniform.  pool_pages > 0:
+// blocks outside [0, pool_pages) are rejected on the device before any access.
 struct PageMeta {
   const int32_t* kv_block;
+  int64_t pool_pages;
   const uint64_t* token_hash;
   const uint64_t* sequence_nonce;
   const uint16_t* layer_id;
@@ -66,8 +71,8 @@ struct MacParams {
   int64_t payload_len;
   int64_t n_pages;
   uint64_t mk0, mk1;
+  PageMeta meta;            // sign mode: block range only (an out-of-range page gets a zero tag)
   // verify mode only
-  PageMeta meta;
   int64_t vecs;
   int64_t head_dim;
   int64_t rope_dim;
@@ -110,6 +115,11 @@ void launch_ingress(const IngressParams& P, cudaStream_t stream);
 void launch_chacha20_xor(const uint8_t* src, uint8_t* dst, int64_t len, const uint32_t key[8], uint32_t counter0,
                          const uint32_t nonce[3], cudaStream_t stream);
 void launch_siphash(const uint8_t* src, int64_t len, uint64_t k0, uint64_t k1, uint8_t* out16, cudaStream_t stream);
+
+// Sets the calling thread's ztcp_last_error message and returns `code` (ztcp_capi.cu).
+int32_t set_last_error(int32_t code, const std::string& msg);
+// Records the phase event armed by ztcp_mark_phase on `stream`, if any, and disarms it (ztcp_measure.cu).
+void take_phase_mark(cudaStream_t stream);
 
 // Staging layout of one tile: 16-byte aligned q and scale areas per section.
 ZTCP_HD int32_t plan_stage(const Layout& L, int32_t tile_vecs, int32_t stage_q[3], int32_t stage_s[3]) {

@@ -30,7 +30,8 @@ def sources() -> list[str]:
 
 def _inputs() -> list[str]:
     return sources() + sorted(glob.glob(os.path.join(CSRC, "*.h")) + glob.glob(os.path.join(CSRC, "*.cuh"))) + [
-        os.path.join(INCLUDE, "ztcp_b200.h"), os.path.join(INCLUDE, "ztcp_ledger.h")
+        os.path.join(INCLUDE, "ztcp_b200.h"), os.path.join(INCLUDE, "ztcp_ledger.h"),
+        os.path.join(INCLUDE, "ztcp_measure.h")
     ]
 
 

@@ -22,6 +22,7 @@ PAGE_AAD_MISMATCH = 2
 PAGE_MAC_FAILED = 3
 PAGE_BAD_FLAGS = 4
 PAGE_TRUNCATED = 5
+PAGE_BAD_BLOCK = 6
 
 # every symbol include/ztcp_b200.h declares
 EXPORTED_SYMBOLS = (
@@ -37,6 +38,9 @@ EXPORTED_SYMBOLS = (
     "ztcp_gather",
     "ztcp_decode_pages_noalloc",
 )
+# every symbol include/ztcp_measure.h declares (measurement entry points, not part of the drop-in boundary)
+MEASURE_SYMBOLS = ("ztcp_measure_int_peaks", "ztcp_mark_phase")
+MEASURE_SCRATCH_BYTES = 8 << 20  # ZTCP_MEASURE_SCRATCH_BYTES
 
 
 class Geometry(C.Structure):
@@ -67,6 +71,18 @@ class PageBatch(C.Structure):
         ("layer_id_uniform", C.c_uint16),
         ("head_group_id", C.c_uint16),
         ("options", C.c_int32),
+        ("kv_pool_pages", C.c_int64),
+    ]
+
+
+class IntPeaks(C.Structure):
+    _fields_ = [
+        ("chacha20_blocks_per_s", C.c_double),
+        ("sip_words_per_s", C.c_double),
+        ("sip_chain_cycles_per_word", C.c_double),
+        ("sip_chain_ms", C.c_double),
+        ("sms", C.c_int32),
+        ("reserved", C.c_int32),
     ]
 
 
@@ -122,6 +138,10 @@ def load() -> C.CDLL:
     L.ztcp_decode_pages_noalloc.restype = i32
     L.ztcp_decode_pages_noalloc.argtypes = [vp, i64, C.POINTER(Geometry), C.POINTER(PageBatch), C.POINTER(Keys), vp,
                                             vp, vp, vp]
+    L.ztcp_measure_int_peaks.restype = i32
+    L.ztcp_measure_int_peaks.argtypes = [vp, i64, C.POINTER(IntPeaks)]
+    L.ztcp_mark_phase.restype = i32
+    L.ztcp_mark_phase.argtypes = [vp]
     L.ztcp_gather.restype = i32
     L.ztcp_gather.argtypes = [vp, i32, C.POINTER(vp), C.POINTER(i32), C.POINTER(i64), i32, vp]
     _lib = L

@@ -52,10 +52,10 @@ def _require_cuda(name: str, t: torch.Tensor, dtypes, device: torch.device | Non
 
 def _page_batch(n_pages: int, token_hashes: torch.Tensor, block_table, sequence_nonces, layer_ids,
                 base_sequence_nonce: int, tenant: int, model: int, layer_id: int, head_group: int,
-                options: int = 0) -> capi.PageBatch:
+                options: int = 0, pool_pages: int = 0) -> capi.PageBatch:
     return capi.PageBatch(n_pages, _ptr(block_table), token_hashes.data_ptr(), _ptr(sequence_nonces), _ptr(layer_ids),
                           int(base_sequence_nonce) & _U64, int(tenant) & 0xFFFFFFFF, int(model) & 0xFFFFFFFF,
-                          int(layer_id) & 0xFFFF, int(head_group) & 0xFFFF, options)
+                          int(layer_id) & 0xFFFF, int(head_group) & 0xFFFF, options, int(pool_pages))
 
 
 def _check_meta(dev, n, block_table, sequence_nonces, layer_ids, token_hashes):
@@ -77,7 +77,9 @@ def _check_meta(dev, n, block_table, sequence_nonces, layer_ids, token_hashes):
 
 
 def _check_block_table(block_table: torch.Tensor | None, pool_pages: int) -> None:
-    # kv_block entries index the pool; a bad entry would address memory outside it.
+    # kv_block entries index the pool.  The kernels check every entry against the pool size on the device
+    # (a bad page is neither read nor written); this host check turns a bad table into an exception before
+    # launch, at the cost of one synchronizing reduction.
     if block_table is not None and block_table.numel() > 0:
         lo, hi = torch.aminmax(block_table)
         if int(lo) < 0 or int(hi) >= pool_pages:
@@ -119,7 +121,7 @@ def encode_pages(k_pool: torch.Tensor, v_pool: torch.Tensor | None, token_hashes
     geom = capi.geometry(T, H, D, rope_dim, v_pool is None)
     batch = _page_batch(n, token_hashes, block_table, sequence_nonces, layer_ids, base_sequence_nonce,
                         tenant_id_hash, model_id_hash, layer_id, head_group_id,
-                        capi.OPT_NEON_ARITH if neon_arith else 0)
+                        capi.OPT_NEON_ARITH if neon_arith else 0, k_pool.shape[0])
     dtype = capi.DTYPE_BF16 if k_pool.dtype == torch.bfloat16 else capi.DTYPE_F16
     rc = _on_device(dev, capi.load().ztcp_encode_pages, k_pool.data_ptr(), _ptr(v_pool), dtype, geom, batch,
                     int(preset), int(rope_mode), int(expected_payload_bytes), keys, out_blobs.data_ptr(),
@@ -163,7 +165,7 @@ def decode_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, out_k: torch.T
     _, T, H, D = out_k.shape
     geom = capi.geometry(T, H, D, rope_dim, is_mla)
     batch = _page_batch(n, token_hashes, block_table, None, layer_ids, 0, tenant_id_hash, model_id_hash,
-                        layer_id, 0, capi.OPT_PAGE_FALLBACK if page_fallback else 0)
+                        layer_id, 0, capi.OPT_PAGE_FALLBACK if page_fallback else 0, out_k.shape[0])
     rc = _on_device(dev, capi.load().ztcp_decode_pages, blobs.data_ptr(), int(blob_bytes), geom, batch, keys,
                     out_k.data_ptr(), _ptr(out_v), status.data_ptr(), any_fail.data_ptr(), _stream_handle(dev))
     capi.check(rc)
@@ -200,6 +202,7 @@ BATCH_MESSAGES = {
     capi.PAGE_TRUNCATED: "KV_INTEGRITY_ERROR: Invalid cold-page header magic, version, or flags",
     capi.PAGE_AAD_MISMATCH: "CROSS_TENANT_CONTAMINATION: Cold-page AAD mismatch",
     capi.PAGE_MAC_FAILED: "KV_INTEGRITY_ERROR: Cold-page MAC verification failed",
+    capi.PAGE_BAD_BLOCK: "block_table entry outside the KV pool (page neither read nor written)",
 }
 SINGLE_MESSAGES = {
     capi.PAGE_BAD_MAGIC: "KV_INTEGRITY_ERROR: Invalid cold-page header magic or version",
@@ -207,6 +210,7 @@ SINGLE_MESSAGES = {
     capi.PAGE_MAC_FAILED: "KV_INTEGRITY_ERROR: Cold-page MAC verification failed",
     capi.PAGE_BAD_FLAGS: "KV_INTEGRITY_ERROR: Invalid cold-page header flags (preset or rope_mode)",
     capi.PAGE_TRUNCATED: "KV_INTEGRITY_ERROR: Cold-page payload truncated for header flags",
+    capi.PAGE_BAD_BLOCK: "block_table entry outside the KV pool (page neither read nor written)",
 }
 
 
