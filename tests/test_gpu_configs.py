@@ -157,7 +157,7 @@ def test_config4_prefix_4096_pages_bit_exact(oracle, preset, payload):
     order = np.random.default_rng(4096).permutation(P).astype(np.int32)   # list position -> pool block
     layers = (np.arange(P) // 64).astype(np.int16)
     m = workload.session_material(31)
-    seqs = ((m["base_seq"] + np.arange(P, dtype=np.uint64)) % 2**64).astype(np.uint64)
+    seqs = np.arange(P, dtype=np.uint64) + np.uint64(m["base_seq"])   # wraps mod 2^64
     toks = workload.token_hashes(P, 4097)
     keys = capi.keys(*m["key"], *m["mac_key"])
     table = torch.from_numpy(order).to(DEV)
