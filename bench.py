@@ -69,7 +69,9 @@ def parse_args():
     ap.add_argument("--no-configs", action="store_true", help="skip the config 1/2/3 legs")
     ap.add_argument("--prefix-pages", type=int, default=4096,
                     help="pages of the full-prefix sweep (benchmark config 4), split over the ranks (0 = skip)")
-    ap.add_argument("--prefix-chunk", type=int, default=256, help="pages per launch in the prefix sweep")
+    ap.add_argument("--prefix-chunk", type=int, default=0,
+                    help="pages per codec call in the prefix sweep (0 = a rank's whole shard in one call per direction; "
+                         "calls of 1,024 pages or more run the egress in wire order)")
     ap.add_argument("--prefix-reps", type=int, default=3)
     return ap.parse_args()
 
@@ -656,7 +658,8 @@ def ours(args):
         pko = torch.empty((pc, 64, 8, 128), dtype=torch.float16, device=dev)
         pvo = torch.empty_like(pko)
         pst = torch.empty(pc, dtype=torch.int32, device=dev)
-        chunks = [(a, min(a + args.prefix_chunk, pc)) for a in range(0, pc, args.prefix_chunk)]
+        step = args.prefix_chunk if args.prefix_chunk > 0 else pc
+        chunks = [(a, min(a + step, pc)) for a in range(0, pc, step)]
         pfail = torch.zeros(max(1, len(chunks)), dtype=torch.int32, device=dev)
         pool = streams[:max(1, min(len(chunks), len(streams)))]
         prefix = {}
@@ -773,8 +776,9 @@ def ours(args):
         if prefix is not None:
             P = args.prefix_pages
             sweep = {"workload": f"cfg4: {P}-page prefix (64 layers x 64 pages of 64x8x128 GQA K+V bf16), seeded "
-                                 f"shuffled block table, contiguous shards over {world} GPU(s), {args.prefix_chunk}-page "
-                                 f"launches on up to {len(pool)} streams per GPU",
+                                 f"shuffled block table, contiguous shards over {world} GPU(s), "
+                                 f"{chunks[0][1] - chunks[0][0]}-page codec calls on up to {len(pool)} stream(s) per GPU"
+                                 + (" (egress in wire order)" if chunks[0][1] - chunks[0][0] >= 1024 else ""),
                      "pages_total": P, "pages_per_gpu": -(-P // world), "hot_bytes": P * PAGE_HOT_BYTES}
             for nm, (te, ti, payload) in prefix.items():
                 sweep[nm] = {"egress_ms": round(te, 4), "ingress_ms": round(ti, 4),

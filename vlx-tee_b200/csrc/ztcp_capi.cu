@@ -7,6 +7,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -97,6 +98,179 @@ int32_t launch_status(const char* what) {
 
 int32_t ztcp::set_last_error(int32_t code, const std::string& msg) { return fail(code, msg); }
 
+// ------------------------------------------------------------------------------------------------
+// Wire-order egress of large batches
+// ------------------------------------------------------------------------------------------------
+// A page's tag is one serial SipHash chain over its blob (~0.6 ms for a cfg0 page), and it can only absorb
+// bytes that are final.  Produced page by page (tile kernel, then chain), a large batch's chains start only
+// once all of its tiles are done, so its egress takes the production time plus a chain.  In wire order --
+// one launch per (section, tile range) of every page, in the blob's byte order -- each launch finalizes the
+// next byte range of every page, and the chains follow it segment by segment on a high-priority side
+// stream, so they run while the rest of the batch is produced: egress takes about max(production, chain).
+// Ordering is by stream events only (no kernel waits on another), and the chain state between segments
+// lives in each blob's header slot (the last segment writes the header), so no memory is allocated.
+namespace {
+
+constexpr int64_t kWireOrderMinPages = 1024;  // 8 chain CTAs; smaller batches gain little over one pass
+constexpr int kMaxLaunches = 16;              // production launches of one wire-order egress
+constexpr int kMaxSideDevices = 64;
+constexpr int32_t kNotWireOrder = 1;          // encode_wire_order: not applicable, take the single pass
+
+struct Launch {
+  int32_t sec, tile_vecs, t0, t1;  // section sec of tiles [t0, t1) (of tile_vecs vecs) in every page
+  int64_t frontier;                // blob bytes [0, frontier) of every page are final once this launch is done
+};
+
+struct ChainSeg {
+  int64_t from, to;  // blob bytes the tag chains absorb
+  int32_t after;     // the production launch whose completion (and all before it) the segment waits for
+};
+
+// Vecs per tile of a one-section launch: about 1,024 groups per CTA, as a whole-page tile of the standard
+// geometry holds, so a CTA's fixed costs weigh the same; staging stays under 96 KB.
+int32_t section_tile_vecs(const ztcp::EgressParams& P, int s) {
+  const ztcp::Section& S = P.L.sec[s];
+  int64_t tv = std::min<int64_t>(std::max<int64_t>(1024 / std::max(S.dim / ztcp::kGroup, 1), 1), P.vecs);
+  while (tv > 1 && tv * (S.q_bpv + S.s_bpv) + 32 > 96 * 1024) tv = (tv + 1) / 2;
+  return (int32_t)tv;
+}
+
+// Production launches in wire order, one per tile of each section's tiling (up to four per section).  Chain
+// segments: the first two launches' bytes one segment each (the chains start as soon as the first launch is
+// done and stay just behind production), then the remaining launches in two segments -- each segment costs
+// ~15-20 us of launch, SM hand-over and ring start-up on top of its words, and production stays ahead of the
+// chains from there on (a 4,096-page cfg0 egress: ~0.52 ms of production on the SMs the chains leave, 0.62 ms
+// of chain).  Returns false when a boundary is not 16-byte aligned (the chains stream whole 16-byte units
+// through their rings).
+bool plan_wire_order(const ztcp::EgressParams& P, Launch L[kMaxLaunches], int* nl, ChainSeg C[kMaxLaunches], int* nc) {
+  const int64_t mac_len = ztcp::kHeaderBytes + P.payload_len;
+  int n = 0;
+  for (int s = 0; s < P.L.n; ++s) {
+    const ztcp::Section& S = P.L.sec[s];
+    const int32_t tv = section_tile_vecs(P, s);
+    const int32_t T = (int32_t)((P.vecs + tv - 1) / tv);
+    const int32_t g = std::min<int32_t>(T, 4);
+    for (int k = 0; k < g; ++k) {
+      const int32_t t0 = (int32_t)((int64_t)T * k / g), t1 = (int32_t)((int64_t)T * (k + 1) / g);
+      if (n == kMaxLaunches) return false;
+      const int64_t frontier = t1 < T ? ztcp::kHeaderBytes + S.q_off + std::min<int64_t>((int64_t)t1 * tv, P.vecs) * S.q_bpv
+                                      : (s + 1 < P.L.n ? ztcp::kHeaderBytes + P.L.sec[s + 1].q_off : mac_len);
+      if (frontier % 16 != 0 && frontier != mac_len) return false;
+      L[n++] = Launch{s, tv, t0, t1, frontier};
+    }
+  }
+  int m = 0;
+  int64_t from = 0;
+  const int rest = n - 2, half = (rest + 1) / 2;
+  for (int j = 0; j < n; ++j) {
+    const bool ends = j < 2 || j == n - 1 || (rest > 1 && j == 1 + half);
+    if (!ends) continue;
+    C[m++] = ChainSeg{from, L[j].frontier, j};
+    from = L[j].frontier;
+  }
+  *nl = n;
+  *nc = m;
+  return m >= 2;
+}
+
+// One production launch with its section's own tiling and staging, no header.
+void section_launch(const ztcp::EgressParams& P, const Launch& l, bool aligned, ztcp::EgressParams* Q) {
+  *Q = P;
+  const int s = l.sec;
+  Q->tile_vecs = l.tile_vecs;
+  Q->n_tiles = (int32_t)((P.vecs + l.tile_vecs - 1) / l.tile_vecs);
+  Q->sec_lo = s;
+  Q->sec_hi = s + 1;
+  Q->tile_lo = l.t0;
+  Q->tiles = l.t1 - l.t0;
+  Q->write_header = 0;
+  const ztcp::Section& S = P.L.sec[s];
+  for (int i = 0; i < 3; ++i) Q->stage_q[i] = Q->stage_s[i] = 0;
+  Q->stage_s[s] = (int32_t)(((int64_t)Q->tile_vecs * S.q_bpv + 15) / 16 * 16);
+  Q->stage_bytes = Q->stage_s[s] + (int32_t)(((int64_t)Q->tile_vecs * S.s_bpv + 15) / 16 * 16);
+  ztcp::build_tile_plan(Q->L, Q->tile_vecs, Q->stage_q, Q->stage_s, aligned, &Q->plan, s, s + 1);
+}
+
+// Per device: the chains' side stream (highest priority), a second production stream (consecutive production
+// launches alternate between the caller's stream and it, so one launch's last wave overlaps the next one's
+// first) and the events that order them.
+struct SideStream {
+  cudaStream_t chain = nullptr, prod = nullptr;
+  cudaEvent_t ev[kMaxLaunches + 3] = {};
+  bool ready = false;
+};
+std::mutex g_side_mu;
+SideStream g_side[kMaxSideDevices];
+
+// The current device's side streams and events, created on first use; null on failure.
+SideStream* side_streams() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxSideDevices) return nullptr;
+  SideStream& S = g_side[dev];
+  if (S.ready) return &S;
+  int least = 0, greatest = 0;
+  cudaDeviceGetStreamPriorityRange(&least, &greatest);
+  if (!S.chain && cudaStreamCreateWithPriority(&S.chain, cudaStreamNonBlocking, greatest) != cudaSuccess) return nullptr;
+  if (!S.prod && cudaStreamCreateWithFlags(&S.prod, cudaStreamNonBlocking) != cudaSuccess) return nullptr;
+  for (auto& e : S.ev)
+    if (!e && cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return nullptr;
+  S.ready = true;
+  return &S;
+}
+
+int32_t encode_wire_order(const ztcp::EgressParams& P, const ztcp::MacParams& M, bool bf16, cudaStream_t s) {
+  Launch L[kMaxLaunches];
+  ChainSeg C[kMaxLaunches];
+  int nl = 0, nc = 0;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(P.out) | (uintptr_t)P.blob_stride) % 16) == 0;
+  if (!aligned || !plan_wire_order(P, L, &nl, C, &nc)) return kNotWireOrder;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cap) != cudaSuccess || cap != cudaStreamCaptureStatusNone) {
+    cudaGetLastError();
+    return kNotWireOrder;  // a captured call stays on the caller's stream
+  }
+  // one call's records and waits are enqueued together: the side streams and events are shared per device
+  std::lock_guard<std::mutex> lock(g_side_mu);
+  SideStream* side = side_streams();
+  if (!side) {
+    cudaGetLastError();
+    return kNotWireOrder;
+  }
+  // ev[j]: production launch j done; ev[nl]: chains done; ev[nl + 1]: call start; ev[nl + 2]: second stream done
+  cudaEvent_t* ev = side->ev;
+  auto record_wait = [](cudaEvent_t e, cudaStream_t from, cudaStream_t to) {
+    if (cudaEventRecord(e, from) != cudaSuccess || cudaStreamWaitEvent(to, e, 0) != cudaSuccess)
+      return launch_status("cudaStreamWaitEvent");
+    return (int32_t)ZTCP_OK;
+  };
+  int32_t rc = record_wait(ev[nl + 1], s, side->prod);  // the second production stream follows the caller's work
+  if (rc != ZTCP_OK) return rc;
+  int c = 0;
+  for (int j = 0; j < nl; ++j) {
+    ztcp::EgressParams Q;
+    section_launch(P, L[j], aligned, &Q);
+    cudaStream_t ps = (j & 1) ? side->prod : s;
+    ztcp::launch_egress(Q, bf16, ps);
+    if ((rc = launch_status("egress_tile_kernel")) != ZTCP_OK) return rc;
+    if ((rc = record_wait(ev[j], ps, side->chain)) != ZTCP_OK) return rc;  // the chains wait for every launch
+    if (c < nc && C[c].after == j) {
+      ztcp::MacParams K = M;
+      K.seg_from = C[c].from;
+      K.seg_to = C[c].to;
+      K.seg_first = c == 0;
+      K.seg_last = c == nc - 1;
+      ztcp::launch_mac_segment(K, side->chain);
+      if ((rc = launch_status("mac_segment_kernel")) != ZTCP_OK) return rc;
+      ++c;
+    }
+  }
+  if ((rc = record_wait(ev[nl + 2], side->prod, s)) != ZTCP_OK) return rc;
+  ztcp::take_phase_mark(s);
+  return record_wait(ev[nl], side->chain, s);
+}
+
+}  // namespace
+
 extern "C" {
 
 const char* ztcp_last_error(void) { return g_last_error.c_str(); }
@@ -165,9 +339,11 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
   }
   if (P.stage_bytes > kMaxStageBytes) return fail(ZTCP_EINVAL, "head_dim too large for one tile");
   if (P.n_pages * P.n_tiles > 0x7FFFFFFFLL) return fail(ZTCP_EINVAL, "batch too large for one launch");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ztcp::launch_egress(P, kv_dtype == ZTCP_DTYPE_BF16, s);
-  if ((rc = launch_status("egress_tile_kernel")) != ZTCP_OK) return rc;
+  P.sec_lo = 0;
+  P.sec_hi = P.L.n;
+  P.tile_lo = 0;
+  P.tiles = P.n_tiles;
+  P.write_header = 1;
 
   ztcp::MacParams M;
   memset(&M, 0, sizeof(M));
@@ -178,6 +354,16 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
   M.mk0 = keys->mac[0];
   M.mk1 = keys->mac[1];
   M.meta = P.meta;
+  M.flags = P.flags;
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool bf16 = kv_dtype == ZTCP_DTYPE_BF16;
+  if (P.n_pages >= kWireOrderMinPages) {
+    rc = encode_wire_order(P, M, bf16, s);
+    if (rc != kNotWireOrder) return rc;
+  }
+  ztcp::launch_egress(P, bf16, s);
+  if ((rc = launch_status("egress_tile_kernel")) != ZTCP_OK) return rc;
   ztcp::take_phase_mark(s);
   ztcp::launch_mac(M, false, s);
   return launch_status("mac_kernel<sign>");

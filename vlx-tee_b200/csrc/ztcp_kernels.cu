@@ -51,11 +51,13 @@ struct Range {
 };
 
 __device__ __forceinline__ int tile_ranges(const Layout& L, int64_t v0, int tv, const int32_t sq[3],
-                                           const int32_t ss[3], bool with_pad, int64_t payload_len, Range r[7]) {
+                                           const int32_t ss[3], bool with_pad, int64_t payload_len, Range r[7],
+                                           int sec_lo, int sec_hi) {
   int n = 0;
 #pragma unroll
   for (int s = 0; s < 3; ++s) {
-    if (s >= L.n) break;
+    if (s >= L.n || s >= sec_hi) break;
+    if (s < sec_lo) continue;
     const Section S = pick(L, s);
     r[n++] = Range{S.q_off + v0 * S.q_bpv, S.q_off + (v0 + tv) * S.q_bpv, sq[s], 0};
     if (S.kind != kRaw) r[n++] = Range{S.s_off + v0 * S.s_bpv, S.s_off + (v0 + tv) * S.s_bpv, ss[s], 0};
@@ -78,8 +80,8 @@ struct RangeTable {
 
 __device__ __forceinline__ void build_range_table(RangeTable& T, const Layout& L, int64_t v0, int tv,
                                                   const int32_t sq[3], const int32_t ss[3], bool with_pad,
-                                                  int64_t payload_len) {
-  T.n = tile_ranges(L, v0, tv, sq, ss, with_pad, payload_len, T.r);
+                                                  int64_t payload_len, int sec_lo = 0, int sec_hi = 3) {
+  T.n = tile_ranges(L, v0, tv, sq, ss, with_pad, payload_len, T.r, sec_lo, sec_hi);
   int64_t acc = 0;
   for (int i = 0; i < T.n; ++i) {
     T.first[i] = acc;
@@ -226,29 +228,33 @@ template <bool BF16, bool NEON>
 __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __grid_constant__ EgressParams P) {
   extern __shared__ __align__(16) uint8_t stage[];
   __shared__ RangeTable T;
-  const int64_t page = blockIdx.x / P.n_tiles;
-  const int tile = (int)(blockIdx.x - page * P.n_tiles);
+  const int64_t page = blockIdx.x / P.tiles;
+  const int tile = P.tile_lo + (int)(blockIdx.x - page * P.tiles);
   const int64_t v0 = (int64_t)tile * P.tile_vecs;
   const int tv = (int)min((int64_t)P.tile_vecs, P.vecs - v0);
-  const bool padded = tile == P.n_tiles - 1 && P.payload_len > P.L.data_end;
+  const bool with_pad = tile == P.n_tiles - 1 && P.sec_hi == P.L.n;  // the last tile of the last section pads
+  const bool padded = with_pad && P.payload_len > P.L.data_end;
   const bool planned = P.plan.ok && tv == P.tile_vecs && !padded;
   const int64_t blk = page_block(P.meta, page);
   uint8_t* blob = P.out + page * P.blob_stride;
   if (blk < 0) {  // block outside the pool: this tile's share of the blob becomes zeros (magic 0)
-    const int64_t chunk = (P.blob_stride + P.n_tiles - 1) / P.n_tiles;
-    const int64_t a = (int64_t)tile * chunk, b = min(a + chunk, P.blob_stride);
-    for (int64_t x = a + threadIdx.x; x < b; x += blockDim.x) blob[x] = 0;
+    if (P.sec_lo == 0) {  // once per tile (a wire-order egress produces the other sections in later launches)
+      const int64_t chunk = (P.blob_stride + P.n_tiles - 1) / P.n_tiles;
+      const int64_t a = (int64_t)tile * chunk, b = min(a + chunk, P.blob_stride);
+      for (int64_t x = a + threadIdx.x; x < b; x += blockDim.x) blob[x] = 0;
+    }
     return;
   }
   if (!planned && threadIdx.x == 0)
-    build_range_table(T, P.L, v0, tv, P.stage_q, P.stage_s, tile == P.n_tiles - 1, P.payload_len);
+    build_range_table(T, P.L, v0, tv, P.stage_q, P.stage_s, with_pad, P.payload_len, P.sec_lo, P.sec_hi);
   const uint16_t* kp = P.k + blk * P.page_elems;
   const uint16_t* vp = P.v ? P.v + blk * P.page_elems : nullptr;
 
-  // ---- phase 1: quantize this tile's rows of every section into shared memory
+  // ---- phase 1: quantize this tile's rows of every section this launch produces into shared memory
 #pragma unroll
   for (int s = 0; s < 3; ++s) {
-    if (s >= P.L.n) break;
+    if (s >= P.sec_hi) break;
+    if (s < P.sec_lo) continue;
     const Section S = P.L.sec[s];
     const SectionTile st{(S.buf ? vp : kp) + v0 * P.head_dim + S.col, stage + P.stage_q[s], stage + P.stage_s[s],
                          P.head_dim, S.q_bpv, S.s_bpv, S.dim >> 4, P.gshift[s], tv};
@@ -257,10 +263,10 @@ __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __gr
     else quantize_section<kRaw, BF16, NEON>(st, P.mul);
   }
 
-  // header (32 bytes) by tile 0
+  // header (32 bytes) by tile 0 (a wire-order egress leaves it to its last tag segment)
   const uint64_t seq = page_seq(P.meta, page);
   const uint16_t layer = page_layer(P.meta, page);
-  if (tile == 0 && threadIdx.x == 0) {
+  if (tile == 0 && threadIdx.x == 0 && P.write_header) {
     const uint64_t tok = P.meta.token_hash[page];
     const uint32_t hw[8] = {(uint32_t)kMagic | ((uint32_t)kVersion << 16) | ((uint32_t)P.flags << 24),
                             P.meta.tenant,
@@ -499,6 +505,134 @@ __global__ void __launch_bounds__(kChainThreads, 1) mac_kernel(const __grid_cons
 }
 
 // ------------------------------------------------------------------------------------------------
+// Tag chains of a wire-order egress, one segment per launch
+// ------------------------------------------------------------------------------------------------
+// Absorbs n_words little-endian words of p (16-byte aligned, or direct loads otherwise) into st and leaves
+// the state clean (the last word folds nothing ahead), so a later launch can continue from it.
+__device__ __forceinline__ void sip_absorb_words(SipState& st, const uint8_t* p, int64_t n_words, uint8_t* ring_ptr) {
+  if (n_words <= 0) return;
+  int64_t i0 = 0;
+  if ((reinterpret_cast<uintptr_t>(p) & 15) == 0 && n_words >= 32) {
+    const int64_t n_chunks = n_words >> 4;
+    const uint32_t ring = (uint32_t)__cvta_generic_to_shared(ring_ptr);
+    auto slot = [&](int64_t c) { return reinterpret_cast<const uint4*>(ring_ptr + (c & (kRing - 1)) * kChunk); };
+#pragma unroll 1
+    for (int c = 0; c < kRing - 1; ++c) ring_fill(ring, p, c, n_chunks);
+    const W64 after = n_chunks * 16 < n_words ? load_word_any(p + n_chunks * kChunk) : W64{0u, 0u};
+    cp_async_wait<kRing - 2>();
+    st.v3 = xor64(st.v3, load_word_any(p));
+#pragma unroll 1
+    for (int64_t c = 0; c < n_chunks; ++c) {
+      ring_fill(ring, p, c + kRing - 1, n_chunks);
+      cp_async_wait<kRing - 2>();
+      const uint4* w = slot(c);
+      const W64 last = c + 1 < n_chunks ? W64{slot(c + 1)[0].x, slot(c + 1)[0].y} : after;
+#pragma unroll 1
+      for (int h = 0; h < 4; ++h) {
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          const int j = 2 * h + jj;
+          const uint4 q = w[j];
+          st.absorb_pre(W64{q.x, q.y}, W64{q.z, q.w});
+          W64 nx;
+          if (j < 7) {
+            const uint4 r = w[j + 1];
+            nx = W64{r.x, r.y};
+          } else {
+            nx = last;
+          }
+          st.absorb_pre(W64{q.z, q.w}, nx);
+        }
+      }
+    }
+    cp_async_wait<0>();
+    i0 = n_chunks * 16;
+    if (i0 == n_words) return;
+  } else {
+    st.v3 = xor64(st.v3, load_word_any(p));
+  }
+  for (int64_t i = i0; i < n_words; ++i)
+    st.absorb_pre(load_word_any(p + 8 * i), i + 1 < n_words ? load_word_any(p + 8 * (i + 1)) : W64{0u, 0u});
+}
+
+__device__ __forceinline__ void header_words(const PageMeta& m, int64_t page, int32_t flags, uint32_t hw[8]) {
+  const uint64_t tok = m.token_hash[page];
+  const uint64_t seq = page_seq(m, page);
+  hw[0] = (uint32_t)kMagic | ((uint32_t)kVersion << 16) | ((uint32_t)flags << 24);
+  hw[1] = m.tenant;
+  hw[2] = m.model;
+  hw[3] = (uint32_t)page_layer(m, page) | ((uint32_t)m.head_group << 16);
+  hw[4] = (uint32_t)tok;
+  hw[5] = (uint32_t)(tok >> 32);
+  hw[6] = (uint32_t)seq;
+  hw[7] = (uint32_t)(seq >> 32);
+}
+
+// One segment of the tag chains (one lane per page, the shape of mac_kernel): blob bytes [seg_from, seg_to)
+// are absorbed after the production launches that write them have finished (stream order).  Between launches a
+// page's chain state (v0..v3, 32 bytes) waits in its blob's header slot, which nothing else reads until the
+// last segment writes the real header there after the tag.
+__global__ void __launch_bounds__(kChainThreads, 1) mac_segment_kernel(const __grid_constant__ MacParams P) {
+  extern __shared__ __align__(16) uint8_t rings[];
+  const int64_t page = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (page >= P.n_pages) return;
+  uint8_t* blob = P.blobs + page * P.blob_stride;
+  const int64_t mac_len = kHeaderBytes + P.payload_len;
+  uint32_t* slot = reinterpret_cast<uint32_t*>(blob);  // 16-byte aligned: checked by the host
+  if (page_block(P.meta, page) < 0) {  // block outside the pool: the blob stays zero (written by the tile kernel)
+    if (P.seg_last)
+      for (int i = 0; i < (int)kTagBytes; ++i) blob[mac_len + i] = 0;
+    return;
+  }
+  SipState st;
+  int64_t from = P.seg_from;
+  if (P.seg_first) {
+    uint32_t hw[8];
+    header_words(P.meta, page, P.flags, hw);
+    st.init(P.mk0, P.mk1);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) st.absorb(hw[2 * i], hw[2 * i + 1]);
+    from = kHeaderBytes;
+  } else {
+    const uint4 a = reinterpret_cast<const uint4*>(slot)[0], b = reinterpret_cast<const uint4*>(slot)[1];
+    st.v0 = W64{a.x, a.y};
+    st.v1 = W64{a.z, a.w};
+    st.v2 = W64{b.x, b.y};
+    st.v3 = W64{b.z, b.w};
+  }
+  const int64_t n_words = (P.seg_to - from) >> 3;
+  sip_absorb_words(st, blob + from, n_words, rings + threadIdx.x * kRingStride);
+  if (!P.seg_last) {
+    reinterpret_cast<uint4*>(slot)[0] = make_uint4(st.v0.lo, st.v0.hi, st.v1.lo, st.v1.hi);
+    reinterpret_cast<uint4*>(slot)[1] = make_uint4(st.v2.lo, st.v2.hi, st.v3.lo, st.v3.hi);
+    return;
+  }
+  // the length word: (mac_len & 0xff) << 56 | the bytes after the last whole word (csrc:425-442)
+  W64 fin{0u, (uint32_t)(mac_len & 0xff) << 24};
+  const uint8_t* t = blob + from + 8 * n_words;
+  const int rem = (int)(P.seg_to - from - 8 * n_words);
+  for (int b = 0; b < rem; ++b) {
+    if (b < 4) fin.lo |= (uint32_t)t[b] << (8 * b);
+    else fin.hi |= (uint32_t)t[b] << (8 * (b - 4));
+  }
+  st.absorb(fin);
+  uint32_t tag[4];
+  st.finish(tag);
+  uint8_t* tag_ptr = blob + mac_len;
+  if ((reinterpret_cast<uintptr_t>(tag_ptr) & 3) == 0) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) reinterpret_cast<uint32_t*>(tag_ptr)[i] = tag[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) tag_ptr[i] = (uint8_t)(tag[i >> 2] >> (8 * (i & 3)));
+  }
+  uint32_t hw[8];
+  header_words(P.meta, page, P.flags, hw);
+  reinterpret_cast<uint4*>(slot)[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+  reinterpret_cast<uint4*>(slot)[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+}
+
+// ------------------------------------------------------------------------------------------------
 // Ingress: decrypt + dequantize one (page, vec-tile), or zero it when the batch failed
 // ------------------------------------------------------------------------------------------------
 // 6 resident CTAs per SM (measured ~9 % faster than the 5 its unconstrained register count allows).
@@ -689,7 +823,7 @@ void ensure_smem(K kernel, int32_t bytes) {
 
 template <bool BF16, bool NEON>
 void launch_egress_t(const EgressParams& P, cudaStream_t stream) {
-  const int64_t grid = P.n_pages * P.n_tiles;
+  const int64_t grid = P.n_pages * P.tiles;
   ensure_smem(egress_tile_kernel<BF16, NEON>, P.stage_bytes);
   egress_tile_kernel<BF16, NEON><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
 }
@@ -723,6 +857,19 @@ void launch_mac(const MacParams& P, bool verify, cudaStream_t stream) {
   }
   if (verify) mac_kernel<true><<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
   else mac_kernel<false><<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
+}
+
+void launch_mac_segment(const MacParams& P, cudaStream_t stream) {
+  const unsigned grid = (unsigned)((P.n_pages + kChainThreads - 1) / kChainThreads);
+  static std::atomic<uint64_t> opted;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = dev < 64 ? (uint64_t)1 << dev : 0;
+  if (!bit || !(opted.load(std::memory_order_relaxed) & bit)) {
+    cudaFuncSetAttribute(mac_segment_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMacReserveBytes);
+    opted.fetch_or(bit, std::memory_order_relaxed);
+  }
+  mac_segment_kernel<<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
 }
 
 void launch_ingress(const IngressParams& P, cudaStream_t stream) {

@@ -62,7 +62,14 @@ struct EgressParams {
   int32_t stage_bytes;
   int32_t neon_arith;       // quantize with the reference's ARM NEON fp16 arithmetic
   PackMul mul;              // integer packing weights {16, 256, 65536}
-  TilePlan plan;            // full tiles of L (blobs 16-byte aligned)
+  TilePlan plan;            // full tiles of L restricted to sections [sec_lo, sec_hi) (blobs 16-byte aligned)
+  // What one launch produces: sections [sec_lo, sec_hi) of tiles [tile_lo, tile_lo + tiles) of every page
+  // (grid = n_pages * tiles).  A whole-page launch is sections [0, L.n) of tiles [0, n_tiles) with the
+  // header; a wire-order egress splits a batch into launches of one section and a tile range each and
+  // leaves the header to its last tag segment.
+  int32_t sec_lo, sec_hi;
+  int32_t tile_lo, tiles;
+  int32_t write_header;
 };
 
 struct MacParams {
@@ -72,6 +79,12 @@ struct MacParams {
   int64_t n_pages;
   uint64_t mk0, mk1;
   PageMeta meta;            // sign mode: block range only (an out-of-range page gets a zero tag)
+  // segment mode (mac_segment_kernel): absorb blob bytes [seg_from, seg_to) into each page's chain; the
+  // state between segments lives in the page's 32-byte header slot; the first segment starts the chain with
+  // the header built from meta, the last one absorbs the length word, writes the tag and then the header
+  int64_t seg_from, seg_to;
+  int32_t seg_first, seg_last;
+  int32_t flags;            // header flags byte (segment mode)
   // verify mode only
   int64_t vecs;
   int64_t head_dim;
@@ -111,6 +124,7 @@ struct IngressParams {
 
 void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream);
 void launch_mac(const MacParams& P, bool verify, cudaStream_t stream);
+void launch_mac_segment(const MacParams& P, cudaStream_t stream);
 void launch_ingress(const IngressParams& P, cudaStream_t stream);
 void launch_chacha20_xor(const uint8_t* src, uint8_t* dst, int64_t len, const uint32_t key[8], uint32_t counter0,
                          const uint32_t nonce[3], cudaStream_t stream);
@@ -135,15 +149,16 @@ ZTCP_HD int32_t plan_stage(const Layout& L, int32_t tile_vecs, int32_t stage_q[3
   return (int32_t)off;
 }
 
-// Tile plan of a layout for full tiles of tile_vecs vecs (see TilePlan); ok stays 0 when a range is not whole
-// 64-byte blocks, block indices would not fit 32 bits, or aligned is false (blobs not 16-byte aligned).
+// Tile plan of a layout for full tiles of tile_vecs vecs and sections [sec_lo, sec_hi) (see TilePlan); ok stays 0
+// when a range is not whole 64-byte blocks, block indices would not fit 32 bits, or aligned is false (blobs not
+// 16-byte aligned).
 ZTCP_HD void build_tile_plan(const Layout& L, int32_t tile_vecs, const int32_t stage_q[3], const int32_t stage_s[3],
-                             bool aligned, TilePlan* T) {
+                             bool aligned, TilePlan* T, int sec_lo = 0, int sec_hi = 3) {
   T->ok = 0;
   T->n = 0;
   int64_t acc = 0;
   bool good = aligned;
-  for (int i = 0; i < L.n && i < 3; ++i) {
+  for (int i = sec_lo; i < L.n && i < sec_hi; ++i) {
     const Section& S = L.sec[i];
     for (int part = 0; part < 2; ++part) {
       if (part == 1 && S.kind == kRaw) break;
