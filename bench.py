@@ -792,7 +792,7 @@ def ours(args):
             line["prefix_sweep"] = sweep
         if cpu_base is not None:
             line["cpu_baseline"] = cpu_base
-        print(json.dumps(line))
+        print(json.dumps(line), file=sys.stdout, flush=True)
     graphs.clear()  # release captured graphs before the process group goes away
     torch.cuda.synchronize()
     if world > 1:

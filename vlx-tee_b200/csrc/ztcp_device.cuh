@@ -171,13 +171,30 @@ __device__ __forceinline__ void load_group16(const uint16_t* src, uint32_t w[8])
 __device__ __forceinline__ uint16_t lo16(uint32_t w) { return (uint16_t)(w & 0xFFFFu); }
 __device__ __forceinline__ uint16_t hi16(uint32_t w) { return (uint16_t)(w >> 16); }
 
-// Largest |x| bit pattern of the group.  For non-negative IEEE halves the bit patterns order like the
-// values, with +inf = 0x7C00 and NaN above it, so a result >= 0x7C00 flags a non-finite element.
+// Largest |x| bit pattern of the group's 16 fp16 (BF16W = false) or bf16 (BF16W = true) elements, as a
+// tree of packed half-precision NaN-propagating maxima of |x| (half the instructions of an integer max of
+// masked bit patterns, and off the integer ALU pipe that ChaCha20 saturates).  For non-negative IEEE halves
+// the bit patterns order like the values, +inf above every finite value and NaN above +inf, so for fp16 a
+// result >= 0x7C00 flags a non-finite element (a NaN anywhere gives a NaN); likewise 0x7F80 for bf16.
+template <bool BF16W>
 __device__ __forceinline__ uint32_t group_amax_bits(const uint32_t w[8]) {
-  uint32_t m = w[0] & 0x7FFF7FFFu;
+  if (BF16W) {
+    __nv_bfloat162 v[8];
 #pragma unroll
-  for (int i = 1; i < 8; ++i) m = __vmaxu2(m, w[i] & 0x7FFF7FFFu);
-  return max(m & 0xFFFFu, m >> 16);
+    for (int i = 0; i < 8; ++i) v[i] = __habs2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+    const __nv_bfloat162 a = __hmax2_nan(__hmax2_nan(v[0], v[1]), __hmax2_nan(v[2], v[3]));
+    const __nv_bfloat162 b = __hmax2_nan(__hmax2_nan(v[4], v[5]), __hmax2_nan(v[6], v[7]));
+    const __nv_bfloat162 m = __hmax2_nan(a, b);
+    return (uint32_t)__bfloat16_as_ushort(__hmax_nan(__low2bfloat16(m), __high2bfloat16(m)));
+  } else {
+    __half2 v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __habs2(*reinterpret_cast<const __half2*>(&w[i]));
+    const __half2 a = __hmax2_nan(__hmax2_nan(v[0], v[1]), __hmax2_nan(v[2], v[3]));
+    const __half2 b = __hmax2_nan(__hmax2_nan(v[4], v[5]), __hmax2_nan(v[6], v[7]));
+    const __half2 m = __hmax2_nan(a, b);
+    return (uint32_t)__half_as_ushort(__hmax_nan(__low2half(m), __high2half(m)));
+  }
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -289,7 +306,7 @@ __device__ __forceinline__ uint32_t pack_int8_word(float e0, float e1, float e2,
 }
 
 __device__ __forceinline__ bool group_scale(const uint32_t w[8], float rq, __half* sh, float* inv) {
-  const uint32_t amax_bits = group_amax_bits(w);
+  const uint32_t amax_bits = group_amax_bits<false>(w);
   if (amax_bits >= 0x7C00u) {  // inf or NaN element: exact path computes everything
     *sh = __float2half_rn(__fmul_rn(amax_exact<8>(w), rq));
     *inv = __frcp_rn(__half2float(*sh));
@@ -352,7 +369,7 @@ __device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w 
 // true when the direct path applied; w holds raw bf16 pairs
 __device__ __forceinline__ bool quant_int4_bf16(const uint32_t w[8], uint32_t q[2], uint16_t* scale,
                                                 const PackMul& mu) {
-  const uint32_t ab = group_amax_bits(w);
+  const uint32_t ab = group_amax_bits<true>(w);
   if (ab < 0x3B00u || ab > kBf16MaxFp16) return false;
   const __half sh = __float2half_rn(__fmul_rn(__uint_as_float(ab << 16), 1.0f / 7.0f));
   const float inv = __frcp_rn(__half2float(sh));
@@ -372,7 +389,7 @@ __device__ __forceinline__ bool quant_int4_bf16(const uint32_t w[8], uint32_t q[
 
 __device__ __forceinline__ bool quant_int8_bf16(const uint32_t w[8], uint32_t q[4], uint16_t* scale,
                                                 const PackMul& mu) {
-  const uint32_t ab = group_amax_bits(w);
+  const uint32_t ab = group_amax_bits<true>(w);
   if (ab < 0x3D00u || ab > kBf16MaxFp16) return false;
   const __half sh = __float2half_rn(__fmul_rn(__uint_as_float(ab << 16), 1.0f / 127.0f));
   const float inv = __frcp_rn(__half2float(sh));
