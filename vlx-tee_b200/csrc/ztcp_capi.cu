@@ -80,14 +80,6 @@ void key_words(const ztcp_keys* k, uint32_t out[8]) {
   }
 }
 
-// Vecs per CTA tile: 64 rows (a whole page when it is smaller), fewer when the staging would exceed
-// 96 KB of shared memory.
-int32_t pick_tile_vecs(int64_t vecs, int64_t stage_per_vec) {
-  int64_t tv = vecs < 64 ? vecs : 64;
-  while (tv > 1 && tv * stage_per_vec > 96 * 1024) tv = (tv + 1) / 2;
-  return (int32_t)tv;
-}
-
 int32_t launch_status(const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(ZTCP_ECUDA, std::string(what) + ": " + cudaGetErrorString(e));
@@ -327,7 +319,7 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
   P.neon_arith = (batch->options & ZTCP_OPT_NEON_ARITH) != 0;
   P.mul = ztcp::PackMul{16u, 256u, 65536u};
   key_words(keys, P.key);
-  P.tile_vecs = pick_tile_vecs(vecs, ztcp::stage_bytes_per_vec(P.L));
+  P.tile_vecs = ztcp::pick_tile_vecs(vecs, ztcp::stage_bytes_per_vec(P.L));
   P.n_tiles = (int32_t)((vecs + P.tile_vecs - 1) / P.tile_vecs);
   P.n_pages = batch->n_pages;
   P.stage_bytes = ztcp::plan_stage(P.L, P.tile_vecs, P.stage_q, P.stage_s);
@@ -335,7 +327,7 @@ int32_t ztcp_encode_pages(const void* k_pages, const void* v_pages, int32_t kv_d
                         (reinterpret_cast<uintptr_t>(P.out) | (uintptr_t)P.blob_stride) % 16 == 0, &P.plan);
   for (int i = 0; i < 3; ++i) {
     const int64_t groups = i < P.L.n ? P.L.sec[i].dim / ztcp::kGroup : 0;
-    P.gshift[i] = (groups > 0 && (groups & (groups - 1)) == 0) ? __builtin_ctzll(groups) : -1;
+    P.gshift[i] = groups > 0 ? ztcp::log2_or_minus1(groups) : -1;
   }
   if (P.stage_bytes > kMaxStageBytes) return fail(ZTCP_EINVAL, "head_dim too large for one tile");
   if (P.n_pages * P.n_tiles > 0x7FFFFFFFLL) return fail(ZTCP_EINVAL, "batch too large for one launch");
@@ -451,7 +443,7 @@ int32_t ztcp_decode_pages(const uint8_t* blobs, int64_t blob_bytes, const ztcp_g
   P.status = status;
   P.page_fallback = (batch->options & ZTCP_OPT_PAGE_FALLBACK) != 0;
   const int64_t worst = ztcp::worst_stage_bytes_per_vec(geom->head_dim, geom->rope_dim, has_v);
-  P.tile_vecs = pick_tile_vecs(vecs, worst);
+  P.tile_vecs = ztcp::pick_tile_vecs(vecs, worst);
   P.n_tiles = (int32_t)((vecs + P.tile_vecs - 1) / P.tile_vecs);
   P.n_pages = batch->n_pages;
   // worst case over every (preset, rope_mode) a header may carry, plus 16-byte rounding per area

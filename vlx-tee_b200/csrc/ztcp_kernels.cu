@@ -220,44 +220,69 @@ __device__ __forceinline__ int32_t log2_if_pow2(int32_t x) {
   return (x > 0 && (x & (x - 1)) == 0) ? __ffs(x) - 1 : -1;
 }
 
+// The compiled geometries' tables (ztcp_kernels.cuh): constant memory the compiler reads at compile time
+// wherever a kernel indexes them with constants.
+__constant__ constexpr StaticEgress kStaticEgress[kStaticEgressCount] = {
+    make_static_egress(kStaticEgressKeys[0][0], kStaticEgressKeys[0][1], kStaticEgressGeometry[0]),
+    make_static_egress(kStaticEgressKeys[1][0], kStaticEgressKeys[1][1], kStaticEgressGeometry[1]),
+    make_static_egress(kStaticEgressKeys[2][0], kStaticEgressKeys[2][1], kStaticEgressGeometry[2])};
+__constant__ constexpr StaticIngress kStaticIngress[kStaticIngressCount] = {
+    make_static_ingress(kStaticIngressGeometry[0]), make_static_ingress(kStaticIngressGeometry[1])};
+
 // ------------------------------------------------------------------------------------------------
 // Egress: quantize + pack + encrypt one (page, vec-tile)
 // ------------------------------------------------------------------------------------------------
 // 7 resident CTAs per SM (the register cap this implies was measured ~5 % faster than 6).
-template <bool BF16, bool NEON>
+// CFG = 0: layout, tiling and staging plan from the launch parameters; CFG = i > 0: those of kStaticEgress[i - 1]
+// as compile-time constants (a whole-batch launch of that geometry and format), so their address and index
+// arithmetic folds away.
+template <bool BF16, bool NEON, int CFG>
 __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __grid_constant__ EgressParams P) {
   extern __shared__ __align__(16) uint8_t stage[];
   __shared__ RangeTable T;
-  const int64_t page = blockIdx.x / P.tiles;
-  const int tile = P.tile_lo + (int)(blockIdx.x - page * P.tiles);
-  const int64_t v0 = (int64_t)tile * P.tile_vecs;
-  const int tv = (int)min((int64_t)P.tile_vecs, P.vecs - v0);
-  const bool with_pad = tile == P.n_tiles - 1 && P.sec_hi == P.L.n;  // the last tile of the last section pads
-  const bool padded = with_pad && P.payload_len > P.L.data_end;
-  const bool planned = P.plan.ok && tv == P.tile_vecs && !padded;
+  const StaticEgress& G = kStaticEgress[CFG > 0 ? CFG - 1 : 0];
+  const Layout& L = CFG ? G.L : P.L;
+  const TilePlan& plan = CFG ? G.plan : P.plan;
+  const int32_t(&stage_q)[3] = CFG ? G.stage_q : P.stage_q;
+  const int32_t(&stage_s)[3] = CFG ? G.stage_s : P.stage_s;
+  const int32_t(&gshift)[3] = CFG ? G.gshift : P.gshift;
+  const int tile_vecs = CFG ? G.tile_vecs : P.tile_vecs;
+  const int n_tiles = CFG ? G.n_tiles : P.n_tiles;
+  const int64_t vecs = CFG ? G.vecs : P.vecs;
+  const int head_dim = CFG ? G.head_dim : P.head_dim;
+  const int64_t page_elems = CFG ? G.page_elems : P.page_elems;
+  const int sec_lo = CFG ? 0 : P.sec_lo, sec_hi = CFG ? G.L.n : P.sec_hi;
+  const int tile_lo = CFG ? 0 : P.tile_lo, tiles = CFG ? G.n_tiles : P.tiles;
+  const int64_t page = blockIdx.x / tiles;
+  const int tile = tile_lo + (int)(blockIdx.x - page * tiles);
+  const int64_t v0 = (int64_t)tile * tile_vecs;
+  const int tv = (int)min((int64_t)tile_vecs, vecs - v0);
+  const bool with_pad = tile == n_tiles - 1 && sec_hi == L.n;  // the last tile of the last section pads
+  const bool padded = with_pad && P.payload_len > L.data_end;
+  const bool planned = plan.ok && tv == tile_vecs && !padded;
   const int64_t blk = page_block(P.meta, page);
   uint8_t* blob = P.out + page * P.blob_stride;
   if (blk < 0) {  // block outside the pool: this tile's share of the blob becomes zeros (magic 0)
-    if (P.sec_lo == 0) {  // once per tile (a wire-order egress produces the other sections in later launches)
-      const int64_t chunk = (P.blob_stride + P.n_tiles - 1) / P.n_tiles;
+    if (sec_lo == 0) {  // once per tile (a wire-order egress produces the other sections in later launches)
+      const int64_t chunk = (P.blob_stride + n_tiles - 1) / n_tiles;
       const int64_t a = (int64_t)tile * chunk, b = min(a + chunk, P.blob_stride);
       for (int64_t x = a + threadIdx.x; x < b; x += blockDim.x) blob[x] = 0;
     }
     return;
   }
   if (!planned && threadIdx.x == 0)
-    build_range_table(T, P.L, v0, tv, P.stage_q, P.stage_s, with_pad, P.payload_len, P.sec_lo, P.sec_hi);
-  const uint16_t* kp = P.k + blk * P.page_elems;
-  const uint16_t* vp = P.v ? P.v + blk * P.page_elems : nullptr;
+    build_range_table(T, L, v0, tv, stage_q, stage_s, with_pad, P.payload_len, sec_lo, sec_hi);
+  const uint16_t* kp = P.k + blk * page_elems;
+  const uint16_t* vp = P.v ? P.v + blk * page_elems : nullptr;
 
   // ---- phase 1: quantize this tile's rows of every section this launch produces into shared memory
 #pragma unroll
   for (int s = 0; s < 3; ++s) {
-    if (s >= P.sec_hi) break;
-    if (s < P.sec_lo) continue;
-    const Section S = P.L.sec[s];
-    const SectionTile st{(S.buf ? vp : kp) + v0 * P.head_dim + S.col, stage + P.stage_q[s], stage + P.stage_s[s],
-                         P.head_dim, S.q_bpv, S.s_bpv, S.dim >> 4, P.gshift[s], tv};
+    if (s >= sec_hi) break;
+    if (s < sec_lo) continue;
+    const Section S = L.sec[s];
+    const SectionTile st{(S.buf ? vp : kp) + v0 * head_dim + S.col, stage + stage_q[s], stage + stage_s[s],
+                         head_dim, S.q_bpv, S.s_bpv, S.dim >> 4, gshift[s], tv};
     if (S.kind == kInt4) quantize_section<kInt4, BF16, NEON>(st, P.mul);
     else if (S.kind == kInt8) quantize_section<kInt8, BF16, NEON>(st, P.mul);
     else quantize_section<kRaw, BF16, NEON>(st, P.mul);
@@ -266,9 +291,9 @@ __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __gr
   // header (32 bytes) by tile 0 (a wire-order egress leaves it to its last tag segment)
   const uint64_t seq = page_seq(P.meta, page);
   const uint16_t layer = page_layer(P.meta, page);
-  if (tile == 0 && threadIdx.x == 0 && P.write_header) {
+  if (tile == 0 && threadIdx.x == 0 && (CFG || P.write_header)) {
     const uint64_t tok = P.meta.token_hash[page];
-    const uint32_t hw[8] = {(uint32_t)kMagic | ((uint32_t)kVersion << 16) | ((uint32_t)P.flags << 24),
+    const uint32_t hw[8] = {(uint32_t)kMagic | ((uint32_t)kVersion << 16) | ((uint32_t)(CFG ? G.flags : P.flags) << 24),
                             P.meta.tenant,
                             P.meta.model,
                             (uint32_t)layer | ((uint32_t)P.meta.head_group << 16),
@@ -290,14 +315,14 @@ __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __gr
   const uint32_t n2 = ((uint32_t)layer << 16) | P.meta.head_group;
   uint8_t* payload = blob + kHeaderBytes;
   if (planned) {  // whole, 16-byte aligned blocks
-    const int total = P.plan.first[P.plan.n];
+    const int total = plan.first[plan.n];
     for (int bi = threadIdx.x; bi < total; bi += blockDim.x) {
-      const int i = plan_range(P.plan, bi);
-      const int rel = bi - P.plan.first[i];
-      const int kb = P.plan.kb0[i] + tile * (P.plan.first[i + 1] - P.plan.first[i]) + rel;
+      const int i = plan_range(plan, bi);
+      const int rel = bi - plan.first[i];
+      const int kb = plan.kb0[i] + tile * (plan.first[i + 1] - plan.first[i]) + rel;
       uint32_t ks[16];
       chacha20_block(P.key, (uint32_t)(1 + kb), (uint32_t)seq, (uint32_t)(seq >> 32), n2, ks);
-      const uint4* src = reinterpret_cast<const uint4*>(stage + P.plan.stage[i] + rel * 64);
+      const uint4* src = reinterpret_cast<const uint4*>(stage + plan.stage[i] + rel * 64);
       uint4* dst = reinterpret_cast<uint4*>(payload + (int64_t)kb * 64);
 #pragma unroll
       for (int w = 0; w < 4; ++w) {
@@ -635,50 +660,15 @@ __global__ void __launch_bounds__(kChainThreads, 1) mac_segment_kernel(const __g
 // ------------------------------------------------------------------------------------------------
 // Ingress: decrypt + dequantize one (page, vec-tile), or zero it when the batch failed
 // ------------------------------------------------------------------------------------------------
-// 6 resident CTAs per SM (measured ~9 % faster than the 5 its unconstrained register count allows).
-__global__ void __launch_bounds__(kTileThreads, 6) ingress_tile_kernel(const __grid_constant__ IngressParams P) {
+// Decrypt + dequantize one verified (page, vec-tile) with layout L, its staging offsets and tile plan: either the
+// launch parameters' entry for the page's flags, or a compile-time one (the same code with constants).
+__device__ __forceinline__ void ingress_tile(const IngressParams& P, RangeTable& T, const Layout& L,
+                                             const int32_t (&sq)[3], const int32_t (&ss)[3], const TilePlan& TP,
+                                             int tile, int64_t v0, int tv, int tile_vecs, int head_dim,
+                                             const uint8_t* payload, uint32_t n0, uint32_t n1, uint32_t n2,
+                                             uint16_t* kd, uint16_t* vd) {
   extern __shared__ __align__(16) uint8_t stage[];
-  const int64_t page = blockIdx.x / P.n_tiles;
-  const int tile = (int)(blockIdx.x - page * P.n_tiles);
-  const int64_t v0 = (int64_t)tile * P.tile_vecs;
-  const int tv = (int)min((int64_t)P.tile_vecs, P.vecs - v0);
-  const int64_t blk = page_block(P.meta, page);
-  if (blk < 0) return;  // block outside the pool: never written (status ZTCP_PAGE_BAD_BLOCK)
-  uint16_t* kd = P.k_out + blk * P.page_elems;
-  uint16_t* vd = P.v_out ? P.v_out + blk * P.page_elems : nullptr;
-
-  if (P.page_fallback ? P.status[page] != 0 : *P.any_fail != 0) {
-    const int64_t n16 = (int64_t)tv * P.head_dim / 8;  // uint4 per buffer
-    uint4* kz = reinterpret_cast<uint4*>(kd + v0 * P.head_dim);
-    uint4* vz = vd ? reinterpret_cast<uint4*>(vd + v0 * P.head_dim) : nullptr;
-    for (int64_t i = threadIdx.x; i < n16; i += blockDim.x) {
-      kz[i] = make_uint4(0, 0, 0, 0);
-      if (vz) vz[i] = make_uint4(0, 0, 0, 0);
-    }
-    return;
-  }
-
-  // header: the flags byte selects the page's layout from the host-built table; nonce words for the
-  // keystream (seq lo, seq hi, layer_id << 16 | head_group_id)
-  const uint8_t* blob = P.blobs + page * P.blob_stride;
-  __shared__ RangeTable T;
-  uint32_t h0, h3, h6, h7;
-  if ((reinterpret_cast<uintptr_t>(blob) & 15) == 0) {
-    const uint4 a = __ldg(reinterpret_cast<const uint4*>(blob));
-    const uint4 b = __ldg(reinterpret_cast<const uint4*>(blob) + 1);
-    h0 = a.x; h3 = a.w; h6 = b.z; h7 = b.w;
-  } else {
-    h0 = ld_u32_any(blob); h3 = ld_u32_any(blob + 12); h6 = ld_u32_any(blob + 24); h7 = ld_u32_any(blob + 28);
-  }
-  const uint32_t flags = h0 >> 24;
-  const int li = (int)((flags & 0x0Fu) - 1u) * 3 + (int)((flags >> 4) & 0x0Fu);
-  const Layout& L = P.lay[li];
-  const int32_t* sq = P.lay_q[li];
-  const int32_t* ss = P.lay_s[li];
-  const TilePlan& TP = P.plan[li];
-  const bool planned = TP.ok && tv == P.tile_vecs;
-  const uint32_t n0 = h6, n1 = h7, n2 = (h3 << 16) | (h3 >> 16);
-  const uint8_t* payload = blob + kHeaderBytes;
+  const bool planned = TP.ok && tv == tile_vecs;
 
   // ---- phase 1: decrypt this tile's byte ranges into shared memory (loads issued before the keystream)
   if (planned) {  // whole, 16-byte aligned blocks
@@ -745,12 +735,74 @@ __global__ void __launch_bounds__(kTileThreads, 6) ingress_tile_kernel(const __g
     if (s >= L.n) break;
     const Section S = L.sec[s];
     const int32_t groups = S.dim >> 4;
-    const SectionTile st{nullptr, stage + sq[s], stage + ss[s], P.head_dim, S.q_bpv, S.s_bpv, groups,
+    const SectionTile st{nullptr, stage + sq[s], stage + ss[s], head_dim, S.q_bpv, S.s_bpv, groups,
                          log2_if_pow2(groups), tv};
-    uint16_t* dst = (S.buf ? vd : kd) + v0 * P.head_dim + S.col;
+    uint16_t* dst = (S.buf ? vd : kd) + v0 * head_dim + S.col;
     if (S.kind == kInt4) dequantize_section<kInt4>(st, dst);
     else if (S.kind == kInt8) dequantize_section<kInt8>(st, dst);
     else dequantize_section<kRaw>(st, dst);
+  }
+}
+
+// 6 resident CTAs per SM (measured ~9 % faster than the 5 its unconstrained register count allows).
+// CFG = 0: geometry, tiling and the layouts of every header flags byte from the launch parameters; CFG = i > 0:
+// those of kStaticIngress[i - 1] as compile-time constants, with the layouts of the formats it lists (the
+// benchmark configurations' flags) each in its own copy of the tile code.
+template <int CFG>
+__global__ void __launch_bounds__(kTileThreads, 6) ingress_tile_kernel(const __grid_constant__ IngressParams P) {
+  __shared__ RangeTable T;
+  const StaticIngress& G = kStaticIngress[CFG > 0 ? CFG - 1 : 0];
+  const int tile_vecs = CFG ? G.tile_vecs : P.tile_vecs;
+  const int n_tiles = CFG ? G.n_tiles : P.n_tiles;
+  const int64_t vecs = CFG ? G.vecs : P.vecs;
+  const int head_dim = CFG ? G.head_dim : P.head_dim;
+  const int64_t page_elems = CFG ? G.page_elems : P.page_elems;
+  const int64_t page = blockIdx.x / n_tiles;
+  const int tile = (int)(blockIdx.x - page * n_tiles);
+  const int64_t v0 = (int64_t)tile * tile_vecs;
+  const int tv = (int)min((int64_t)tile_vecs, vecs - v0);
+  const int64_t blk = page_block(P.meta, page);
+  if (blk < 0) return;  // block outside the pool: never written (status ZTCP_PAGE_BAD_BLOCK)
+  uint16_t* kd = P.k_out + blk * page_elems;
+  uint16_t* vd = P.v_out ? P.v_out + blk * page_elems : nullptr;
+
+  if (P.page_fallback ? P.status[page] != 0 : *P.any_fail != 0) {
+    const int64_t n16 = (int64_t)tv * head_dim / 8;  // uint4 per buffer
+    uint4* kz = reinterpret_cast<uint4*>(kd + v0 * head_dim);
+    uint4* vz = vd ? reinterpret_cast<uint4*>(vd + v0 * head_dim) : nullptr;
+    for (int64_t i = threadIdx.x; i < n16; i += blockDim.x) {
+      kz[i] = make_uint4(0, 0, 0, 0);
+      if (vz) vz[i] = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+
+  // header: the flags byte selects the page's layout; nonce words for the keystream (seq lo, seq hi,
+  // layer_id << 16 | head_group_id)
+  const uint8_t* blob = P.blobs + page * P.blob_stride;
+  uint32_t h0, h3, h6, h7;
+  if ((reinterpret_cast<uintptr_t>(blob) & 15) == 0) {
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(blob));
+    const uint4 b = __ldg(reinterpret_cast<const uint4*>(blob) + 1);
+    h0 = a.x; h3 = a.w; h6 = b.z; h7 = b.w;
+  } else {
+    h0 = ld_u32_any(blob); h3 = ld_u32_any(blob + 12); h6 = ld_u32_any(blob + 24); h7 = ld_u32_any(blob + 28);
+  }
+  const uint32_t flags = h0 >> 24;
+  const int li = (int)((flags & 0x0Fu) - 1u) * 3 + (int)((flags >> 4) & 0x0Fu);
+  const uint32_t n0 = h6, n1 = h7, n2 = (h3 << 16) | (h3 >> 16);
+  const uint8_t* payload = blob + kHeaderBytes;
+  if (CFG && li == kStaticIngressFast0) {
+    constexpr int F = kStaticIngressFast0;
+    ingress_tile(P, T, G.lay[F], G.lay_q[F], G.lay_s[F], G.plan[F], tile, v0, tv, tile_vecs, head_dim, payload,
+                 n0, n1, n2, kd, vd);
+  } else if (CFG && li == kStaticIngressFast1) {
+    constexpr int F = kStaticIngressFast1;
+    ingress_tile(P, T, G.lay[F], G.lay_q[F], G.lay_s[F], G.plan[F], tile, v0, tv, tile_vecs, head_dim, payload,
+                 n0, n1, n2, kd, vd);
+  } else {
+    ingress_tile(P, T, P.lay[li], P.lay_q[li], P.lay_s[li], P.plan[li], tile, v0, tv, tile_vecs, head_dim, payload,
+                 n0, n1, n2, kd, vd);
   }
 }
 
@@ -821,20 +873,91 @@ void ensure_smem(K kernel, int32_t bytes) {
 
 }  // namespace
 
-template <bool BF16, bool NEON>
+namespace {
+
+// Host copies of the compiled tables (the same compile-time values), for matching launches against them.
+constexpr StaticEgress kStaticEgressHost[kStaticEgressCount] = {
+    make_static_egress(kStaticEgressKeys[0][0], kStaticEgressKeys[0][1], kStaticEgressGeometry[0]),
+    make_static_egress(kStaticEgressKeys[1][0], kStaticEgressKeys[1][1], kStaticEgressGeometry[1]),
+    make_static_egress(kStaticEgressKeys[2][0], kStaticEgressKeys[2][1], kStaticEgressGeometry[2])};
+constexpr StaticIngress kStaticIngressHost[kStaticIngressCount] = {
+    make_static_ingress(kStaticIngressGeometry[0]), make_static_ingress(kStaticIngressGeometry[1])};
+
+bool same(const Section& a, const Section& b) {
+  return a.kind == b.kind && a.buf == b.buf && a.col == b.col && a.dim == b.dim && a.q_off == b.q_off &&
+         a.s_off == b.s_off && a.q_bpv == b.q_bpv && a.s_bpv == b.s_bpv;
+}
+bool same(const Layout& a, const Layout& b) {
+  if (a.n != b.n || a.data_end != b.data_end) return false;
+  for (int i = 0; i < a.n; ++i)
+    if (!same(a.sec[i], b.sec[i])) return false;
+  return true;
+}
+bool same(const TilePlan& a, const TilePlan& b) {
+  if (a.ok != b.ok || a.n != b.n) return false;
+  if (!a.ok) return true;
+  for (int i = 0; i <= a.n; ++i)
+    if (a.first[i] != b.first[i]) return false;
+  for (int i = 0; i < a.n; ++i)
+    if (a.kb0[i] != b.kb0[i] || a.stage[i] != b.stage[i]) return false;
+  return true;
+}
+bool same3(const int32_t (&a)[3], const int32_t (&b)[3]) { return a[0] == b[0] && a[1] == b[1] && a[2] == b[2]; }
+
+template <bool BF16, bool NEON, int CFG>
 void launch_egress_t(const EgressParams& P, cudaStream_t stream) {
   const int64_t grid = P.n_pages * P.tiles;
-  ensure_smem(egress_tile_kernel<BF16, NEON>, P.stage_bytes);
-  egress_tile_kernel<BF16, NEON><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+  ensure_smem(egress_tile_kernel<BF16, NEON, CFG>, P.stage_bytes);
+  egress_tile_kernel<BF16, NEON, CFG><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+}
+
+template <bool BF16>
+void launch_egress_x86(const EgressParams& P, cudaStream_t stream) {
+  switch (static_egress_index(P)) {
+    case 1: launch_egress_t<BF16, false, 1>(P, stream); break;
+    case 2: launch_egress_t<BF16, false, 2>(P, stream); break;
+    case 3: launch_egress_t<BF16, false, 3>(P, stream); break;
+    default: launch_egress_t<BF16, false, 0>(P, stream); break;
+  }
+}
+
+}  // namespace
+
+int static_egress_index(const EgressParams& P) {
+  if (P.neon_arith || P.sec_lo != 0 || P.sec_hi != P.L.n || P.tile_lo != 0 || P.tiles != P.n_tiles || !P.write_header)
+    return 0;
+  for (int i = 0; i < kStaticEgressCount; ++i) {
+    const StaticEgress& S = kStaticEgressHost[i];
+    if (P.vecs == S.vecs && P.head_dim == S.head_dim && P.page_elems == S.page_elems && P.flags == S.flags &&
+        P.tile_vecs == S.tile_vecs && P.n_tiles == S.n_tiles && P.stage_bytes == S.stage_bytes && same(P.L, S.L) &&
+        same(P.plan, S.plan) && same3(P.stage_q, S.stage_q) && same3(P.stage_s, S.stage_s) && same3(P.gshift, S.gshift))
+      return i + 1;
+  }
+  return 0;
+}
+
+int static_ingress_index(const IngressParams& P) {
+  for (int i = 0; i < kStaticIngressCount; ++i) {
+    const StaticIngress& S = kStaticIngressHost[i];
+    if (P.vecs != S.vecs || P.head_dim != S.head_dim || P.page_elems != S.page_elems || P.has_v != S.has_v ||
+        P.tile_vecs != S.tile_vecs || P.n_tiles != S.n_tiles || P.stage_bytes != S.stage_bytes)
+      continue;
+    bool eq = true;
+    for (int l = 0; l < 9 && eq; ++l)
+      eq = same(P.lay[l], S.lay[l]) && same(P.plan[l], S.plan[l]) && same3(P.lay_q[l], S.lay_q[l]) &&
+           same3(P.lay_s[l], S.lay_s[l]);
+    if (eq) return i + 1;
+  }
+  return 0;
 }
 
 void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream) {
   if (P.neon_arith) {
-    if (bf16) launch_egress_t<true, true>(P, stream);
-    else launch_egress_t<false, true>(P, stream);
+    if (bf16) launch_egress_t<true, true, 0>(P, stream);
+    else launch_egress_t<false, true, 0>(P, stream);
   } else {
-    if (bf16) launch_egress_t<true, false>(P, stream);
-    else launch_egress_t<false, false>(P, stream);
+    if (bf16) launch_egress_x86<true>(P, stream);
+    else launch_egress_x86<false>(P, stream);
   }
 }
 
@@ -872,10 +995,23 @@ void launch_mac_segment(const MacParams& P, cudaStream_t stream) {
   mac_segment_kernel<<<grid, kChainThreads, kMacReserveBytes, stream>>>(P);
 }
 
-void launch_ingress(const IngressParams& P, cudaStream_t stream) {
+namespace {
+
+template <int CFG>
+void launch_ingress_t(const IngressParams& P, cudaStream_t stream) {
   const int64_t grid = P.n_pages * P.n_tiles;
-  ensure_smem(ingress_tile_kernel, P.stage_bytes);
-  ingress_tile_kernel<<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+  ensure_smem(ingress_tile_kernel<CFG>, P.stage_bytes);
+  ingress_tile_kernel<CFG><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+}
+
+}  // namespace
+
+void launch_ingress(const IngressParams& P, cudaStream_t stream) {
+  switch (static_ingress_index(P)) {
+    case 1: launch_ingress_t<1>(P, stream); break;
+    case 2: launch_ingress_t<2>(P, stream); break;
+    default: launch_ingress_t<0>(P, stream); break;
+  }
 }
 
 void launch_chacha20_xor(const uint8_t* src, uint8_t* dst, int64_t len, const uint32_t key[8], uint32_t counter0,

@@ -33,11 +33,11 @@ constexpr int kTileThreads = 256;
 // so a CTA maps a block to its range by comparisons instead of a table that one thread builds while the
 // others wait.  ok == 0: the kernels take the general path (ragged or unaligned ranges, padded tails).
 struct TilePlan {
-  int32_t ok;
-  int32_t n;
-  int32_t first[7];
-  int32_t kb0[6];
-  int32_t stage[6];
+  int32_t ok = 0;
+  int32_t n = 0;
+  int32_t first[7] = {};
+  int32_t kb0[6] = {};
+  int32_t stage[6] = {};
 };
 
 struct EgressParams {
@@ -176,5 +176,105 @@ ZTCP_HD void build_tile_plan(const Layout& L, int32_t tile_vecs, const int32_t s
   if (L.data_end / 64 > 0x3FFFFFFF) good = false;
   T->ok = good && T->n > 0 ? 1 : 0;
 }
+
+// Vecs per CTA tile: 64 rows (a whole page when it is smaller), fewer when the staging would exceed
+// 96 KB of shared memory.
+ZTCP_HD int32_t pick_tile_vecs(int64_t vecs, int64_t stage_per_vec) {
+  int64_t tv = vecs < 64 ? vecs : 64;
+  while (tv > 1 && tv * stage_per_vec > 96 * 1024) tv = (tv + 1) / 2;
+  return (int32_t)tv;
+}
+
+ZTCP_HD int32_t log2_or_minus1(int64_t x) {
+  if (x <= 0 || (x & (x - 1)) != 0) return -1;
+  int32_t k = 0;
+  while (((int64_t)1 << k) < x) ++k;
+  return k;
+}
+
+// ------------------------------------------------------------------------------------------------
+// Page geometries compiled into their own tile kernels
+// ------------------------------------------------------------------------------------------------
+// The tile kernels read the wire layout, tiling and staging plan of a launch from their parameters, which costs
+// address and index arithmetic on every group and keystream block.  For the benchmark configurations' page
+// geometries and formats the same values are also compile-time constants: a second instantiation of each tile
+// kernel reads them from a table the compiler folds, and the launchers pick it when a launch's parameters equal a
+// table entry (the generic kernel otherwise).  The values are computed by the same functions the host uses.
+struct StaticGeometry {
+  int32_t num_tokens = 0, num_heads = 0, head_dim = 0, rope_dim = 0;
+  bool has_v = false;
+};
+constexpr StaticGeometry kGqa64x8x128{64, 8, 128, 64, true};    // benchmark configurations 0, 1, 2, 4
+constexpr StaticGeometry kMla64x1x576{64, 1, 576, 64, false};   // benchmark configuration 3
+
+// Egress: a whole-batch launch (every section and tile, with the header) of one format and geometry.
+struct StaticEgress {
+  Layout L{};
+  TilePlan plan{};
+  int32_t stage_q[3] = {}, stage_s[3] = {}, gshift[3] = {};
+  int32_t tile_vecs = 0, n_tiles = 0, head_dim = 0, flags = 0, stage_bytes = 0;
+  int64_t vecs = 0, page_elems = 0;
+};
+
+ZTCP_HD StaticEgress make_static_egress(int preset, int rope_mode, StaticGeometry g) {
+  StaticEgress e{};
+  e.vecs = (int64_t)g.num_tokens * g.num_heads;
+  e.head_dim = g.head_dim;
+  e.page_elems = e.vecs * g.head_dim;
+  e.flags = (preset & 0x0F) | ((rope_mode & 0x0F) << 4);
+  build_layout(preset, rope_mode, e.vecs, g.head_dim, g.rope_dim, g.has_v, &e.L);
+  e.tile_vecs = pick_tile_vecs(e.vecs, stage_bytes_per_vec(e.L));
+  e.n_tiles = (int32_t)((e.vecs + e.tile_vecs - 1) / e.tile_vecs);
+  e.stage_bytes = plan_stage(e.L, e.tile_vecs, e.stage_q, e.stage_s);
+  build_tile_plan(e.L, e.tile_vecs, e.stage_q, e.stage_s, true, &e.plan);
+  for (int i = 0; i < 3; ++i) e.gshift[i] = i < e.L.n ? log2_or_minus1(e.L.sec[i].dim / kGroup) : -1;
+  return e;
+}
+
+// (preset, rope_mode) and geometry of each compiled egress: INT4_SYM and K8V4_ASYM with PRESERVE_FP8 on GQA
+// pages, INT4_SYM with PRESERVE_FP8 on MLA pages.
+constexpr int kStaticEgressCount = 3;
+constexpr int kStaticEgressKeys[kStaticEgressCount][2] = {{1, 1}, {2, 1}, {1, 1}};
+constexpr StaticGeometry kStaticEgressGeometry[kStaticEgressCount] = {kGqa64x8x128, kGqa64x8x128, kMla64x1x576};
+
+// Ingress: a geometry with the layouts of every flags byte a header may carry, two of them (the benchmark
+// formats) compiled into their own copies of the tile code.
+struct StaticIngress {
+  Layout lay[9] = {};
+  int32_t lay_q[9][3] = {}, lay_s[9][3] = {};
+  TilePlan plan[9] = {};
+  int32_t tile_vecs = 0, n_tiles = 0, head_dim = 0, has_v = 0, stage_bytes = 0;
+  int64_t vecs = 0, page_elems = 0;
+};
+
+ZTCP_HD StaticIngress make_static_ingress(StaticGeometry g) {
+  StaticIngress s{};
+  s.vecs = (int64_t)g.num_tokens * g.num_heads;
+  s.head_dim = g.head_dim;
+  s.page_elems = s.vecs * g.head_dim;
+  s.has_v = g.has_v ? 1 : 0;
+  const int64_t worst = worst_stage_bytes_per_vec(g.head_dim, g.rope_dim, g.has_v);
+  s.tile_vecs = pick_tile_vecs(s.vecs, worst);
+  s.n_tiles = (int32_t)((s.vecs + s.tile_vecs - 1) / s.tile_vecs);
+  s.stage_bytes = (int32_t)(s.tile_vecs * worst + 6 * 16);
+  for (int p = 1; p <= 3; ++p)
+    for (int r = 0; r <= 2; ++r) {
+      const int i = (p - 1) * 3 + r;
+      build_layout(p, r, s.vecs, g.head_dim, g.rope_dim, g.has_v, &s.lay[i]);
+      plan_stage(s.lay[i], s.tile_vecs, s.lay_q[i], s.lay_s[i]);
+      build_tile_plan(s.lay[i], s.tile_vecs, s.lay_q[i], s.lay_s[i], true, &s.plan[i]);
+    }
+  return s;
+}
+
+constexpr int kStaticIngressCount = 2;
+constexpr StaticGeometry kStaticIngressGeometry[kStaticIngressCount] = {kGqa64x8x128, kMla64x1x576};
+// layout indices ((preset - 1) * 3 + rope_mode) with their own copy of the ingress tile code:
+// INT4_SYM + PRESERVE_FP8 and K8V4_ASYM + PRESERVE_FP8
+constexpr int kStaticIngressFast0 = 1, kStaticIngressFast1 = 4;
+
+// Index + 1 of the compiled egress / ingress whose values a launch's parameters equal, or 0.
+int static_egress_index(const EgressParams& P);
+int static_ingress_index(const IngressParams& P);
 
 }  // namespace ztcp

@@ -17,9 +17,9 @@
 #include <stdint.h>
 
 #if defined(__CUDACC__)
-#define ZTCP_HD __host__ __device__ __forceinline__
+#define ZTCP_HD constexpr __host__ __device__ __forceinline__
 #else
-#define ZTCP_HD inline
+#define ZTCP_HD constexpr inline
 #endif
 
 namespace ztcp {
@@ -39,20 +39,20 @@ struct PackMul {
 };
 
 struct Section {
-  int32_t kind;    // SectionKind
-  int32_t buf;     // 0 = K, 1 = V
-  int32_t col;     // first source column
-  int32_t dim;     // number of source columns (multiple of 16)
-  int64_t q_off;   // payload offset of the q (or raw) region
-  int64_t s_off;   // payload offset of the scale region (== end of the q region)
-  int32_t q_bpv;   // q bytes per vec (raw: dim*2, int8: dim, int4: dim/2)
-  int32_t s_bpv;   // scale bytes per vec (groups*2; 0 for raw)
+  int32_t kind = 0;   // SectionKind
+  int32_t buf = 0;    // 0 = K, 1 = V
+  int32_t col = 0;    // first source column
+  int32_t dim = 0;    // number of source columns (multiple of 16)
+  int64_t q_off = 0;  // payload offset of the q (or raw) region
+  int64_t s_off = 0;  // payload offset of the scale region (== end of the q region)
+  int32_t q_bpv = 0;  // q bytes per vec (raw: dim*2, int8: dim, int4: dim/2)
+  int32_t s_bpv = 0;  // scale bytes per vec (groups*2; 0 for raw)
 };
 
 struct Layout {
-  int32_t n;          // number of sections (0..3)
-  Section sec[3];
-  int64_t data_end;   // first payload byte after the last section (minimum payload)
+  int32_t n = 0;          // number of sections (0..3)
+  Section sec[3] = {};
+  int64_t data_end = 0;   // first payload byte after the last section (minimum payload)
 };
 
 // Section walk for (preset, rope_mode) -- csrc:1376-1409 and required_payload_bytes_for_flags
@@ -89,7 +89,7 @@ ZTCP_HD bool build_layout(int preset, int rope_mode, int64_t vecs, int64_t head_
 // rounded up to a 4-byte multiple.  Returns -1 for invalid flags.
 ZTCP_HD int64_t spec_payload_bytes(int preset, int rope_mode, int64_t vecs, int64_t head_dim,
                                    int64_t rope_dim, bool has_v) {
-  Layout L;
+  Layout L{};
   if (!build_layout(preset, rope_mode, vecs, head_dim, rope_dim, has_v, &L)) return -1;
   return (L.data_end + 3) / 4 * 4;
 }
@@ -107,7 +107,7 @@ ZTCP_HD int64_t worst_stage_bytes_per_vec(int64_t head_dim, int64_t rope_dim, bo
   int64_t worst = 0;
   for (int p = 1; p <= 3; ++p)
     for (int r = 0; r <= 2; ++r) {
-      Layout L;
+      Layout L{};
       build_layout(p, r, 1, head_dim, rope_dim, has_v, &L);
       int64_t b = stage_bytes_per_vec(L);
       if (b > worst) worst = b;
