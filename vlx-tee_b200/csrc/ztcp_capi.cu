@@ -185,7 +185,8 @@ void section_launch(const ztcp::EgressParams& P, const Launch& l, bool aligned, 
 
 // Per device: the chains' side stream (highest priority), a second production stream (consecutive production
 // launches alternate between the caller's stream and it, so one launch's last wave overlaps the next one's
-// first) and the events that order them.
+// first) and the events that order them.  Created on a device's first wire-order egress and kept until the
+// process exits (driver objects, no device memory of the caller's).
 struct SideStream {
   cudaStream_t chain = nullptr, prod = nullptr;
   cudaEvent_t ev[kMaxLaunches + 3] = {};
@@ -237,14 +238,25 @@ int32_t encode_wire_order(const ztcp::EgressParams& P, const ztcp::MacParams& M,
   };
   int32_t rc = record_wait(ev[nl + 1], s, side->prod);  // the second production stream follows the caller's work
   if (rc != ZTCP_OK) return rc;
+  // On a failure after the first launch, the caller's stream still waits for what the side streams hold, so no
+  // work of this call runs after the caller's next operation on its buffers.
+  auto fail_joined = [&](int32_t code) {
+    const std::string msg = g_last_error;
+    cudaEventRecord(ev[nl + 2], side->prod);
+    cudaStreamWaitEvent(s, ev[nl + 2], 0);
+    cudaEventRecord(ev[nl], side->chain);
+    cudaStreamWaitEvent(s, ev[nl], 0);
+    g_last_error = msg;
+    return code;
+  };
   int c = 0;
   for (int j = 0; j < nl; ++j) {
     ztcp::EgressParams Q;
     section_launch(P, L[j], aligned, &Q);
     cudaStream_t ps = (j & 1) ? side->prod : s;
     ztcp::launch_egress(Q, bf16, ps);
-    if ((rc = launch_status("egress_tile_kernel")) != ZTCP_OK) return rc;
-    if ((rc = record_wait(ev[j], ps, side->chain)) != ZTCP_OK) return rc;  // the chains wait for every launch
+    if ((rc = launch_status("egress_tile_kernel")) != ZTCP_OK) return fail_joined(rc);
+    if ((rc = record_wait(ev[j], ps, side->chain)) != ZTCP_OK) return fail_joined(rc);  // the chains wait for every launch
     if (c < nc && C[c].after == j) {
       ztcp::MacParams K = M;
       K.seg_from = C[c].from;
@@ -252,13 +264,14 @@ int32_t encode_wire_order(const ztcp::EgressParams& P, const ztcp::MacParams& M,
       K.seg_first = c == 0;
       K.seg_last = c == nc - 1;
       ztcp::launch_mac_segment(K, side->chain);
-      if ((rc = launch_status("mac_segment_kernel")) != ZTCP_OK) return rc;
+      if ((rc = launch_status("mac_segment_kernel")) != ZTCP_OK) return fail_joined(rc);
       ++c;
     }
   }
-  if ((rc = record_wait(ev[nl + 2], side->prod, s)) != ZTCP_OK) return rc;
+  if ((rc = record_wait(ev[nl + 2], side->prod, s)) != ZTCP_OK) return fail_joined(rc);
   ztcp::take_phase_mark(s);
-  return record_wait(ev[nl], side->chain, s);
+  if ((rc = record_wait(ev[nl], side->chain, s)) != ZTCP_OK) return fail_joined(rc);
+  return ZTCP_OK;
 }
 
 }  // namespace
