@@ -91,3 +91,33 @@ def test_wire_order_then_decode_round_trip():
                            base_sequence_nonce=(m["base_seq"] + a) % 2**64, keys=keys)
     torch.cuda.synchronize()
     assert torch.equal(blobs, b2)
+
+
+def test_captured_large_encode_takes_the_single_pass():
+    """A 1,024-page encode captured into a CUDA graph stays on the capturing stream (single pass) and replays
+    the same bytes as the eager call, which runs in wire order on the library's side streams."""
+    from ztcp_b200 import capi, codec, workload
+
+    n = 1024
+    k, v = workload.kv_pages_torch(n, workload.GQA, seed=91, device=DEV)
+    m = workload.session_material(92)
+    keys = capi.keys(*m["key"], *m["mac_key"])
+    toks = torch.from_numpy(workload.token_hashes(n, 93)).to(DEV)
+
+    def enc(out):
+        codec.encode_pages(k, v, toks, out, rope_dim=64, preset=1, rope_mode=1, expected_payload_bytes=98304,
+                           tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"],
+                           head_group_id=m["head_group"], base_sequence_nonce=m["base_seq"], keys=keys)
+
+    eager = torch.empty((n, 98352), dtype=torch.uint8, device=DEV)
+    enc(eager)
+    replayed = torch.zeros_like(eager)
+    s = torch.cuda.Stream(device=DEV)
+    s.wait_stream(torch.cuda.current_stream(DEV))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=s):
+        enc(replayed)
+    g.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(eager, replayed)
+    del g
