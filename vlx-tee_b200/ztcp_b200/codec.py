@@ -29,12 +29,45 @@ def _stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+def _stream_arg(device: torch.device, stream) -> int:
+    """Raw handle of `stream` (a torch.cuda.Stream on `device`, a raw handle, or None for the current stream)."""
+    if stream is None:
+        return _stream_handle(device)
+    if isinstance(stream, int):
+        return stream
+    if stream.device != device:
+        raise RuntimeError(f"stream must be on {device}, got {stream.device}")
+    return stream.cuda_stream
+
+
 def _on_device(device: torch.device, fn, *args):
     """Call fn(*args) with `device` current (the C-ABI launches on the current device)."""
     if torch.cuda.current_device() == device.index:
         return fn(*args)
     with torch.cuda.device(device):
         return fn(*args)
+
+
+class PreparedCall:
+    """A codec call checked once, with its C-ABI argument blocks built once: calling it enqueues the same
+    kernels on `stream` (a torch.cuda.Stream, a raw handle, or None for the current stream) and returns the
+    call's device outputs (None for an egress, (status, any_fail) for a decode or verify).
+
+    The tensors are kept alive by the object and read at every call, so their contents may change between
+    calls (new K/V, blobs, token hashes or block-table entries); their shapes, devices and addresses may not.
+    A block table's entries are checked on the host when the call is prepared and on the device at every
+    call (an entry outside the pool fails that page with PAGE_BAD_BLOCK and touches no memory)."""
+
+    __slots__ = ("_fn", "_args", "_dev", "_keep", "_result")
+
+    def __init__(self, fn, args, dev, keep, result=None):
+        self._fn, self._args, self._dev, self._keep, self._result = fn, args, dev, keep, result
+
+    def __call__(self, stream=None):
+        rc = _on_device(self._dev, self._fn, *self._args, _stream_arg(self._dev, stream))
+        if rc != capi.ZTCP_OK:
+            capi.check(rc)
+        return self._result
 
 
 def _require_cuda(name: str, t: torch.Tensor, dtypes, device: torch.device | None = None) -> None:
@@ -87,16 +120,29 @@ def _check_block_table(block_table: torch.Tensor | None, pool_pages: int) -> Non
 
 
 def encode_pages(k_pool: torch.Tensor, v_pool: torch.Tensor | None, token_hashes: torch.Tensor,
-                 out_blobs: torch.Tensor, *, rope_dim: int, preset: int, rope_mode: int, expected_payload_bytes: int,
-                 tenant_id_hash: int, model_id_hash: int, layer_id: int, head_group_id: int,
-                 base_sequence_nonce: int, keys: capi.Keys, block_table: torch.Tensor | None = None,
-                 sequence_nonces: torch.Tensor | None = None, layer_ids: torch.Tensor | None = None,
-                 check_block_table: bool = True, neon_arith: bool = False) -> None:
-    """Egress of ``out_blobs.shape[0]`` pages from a KV pool [pool_pages, T, H, D] (fp16 or bf16).
+                 out_blobs: torch.Tensor, *, stream=None, **kw) -> None:
+    """Egress of ``out_blobs.shape[0]`` pages from a KV pool [pool_pages, T, H, D] (fp16 or bf16), enqueued
+    on `stream` (default: the current stream); keyword arguments as for ``prepare_encode``."""
+    prepare_encode(k_pool, v_pool, token_hashes, out_blobs, **kw)(stream)
+
+
+def prepare_encode(k_pool: torch.Tensor, v_pool: torch.Tensor | None, token_hashes: torch.Tensor,
+                   out_blobs: torch.Tensor, *, rope_dim: int, preset: int, rope_mode: int, expected_payload_bytes: int,
+                   tenant_id_hash: int, model_id_hash: int, layer_id: int, head_group_id: int,
+                   base_sequence_nonce: int, keys: capi.Keys, block_table: torch.Tensor | None = None,
+                   sequence_nonces: torch.Tensor | None = None, layer_ids: torch.Tensor | None = None,
+                   check_block_table: bool = True, neon_arith: bool = False) -> PreparedCall:
+    """Egress of ``out_blobs.shape[0]`` pages from a KV pool [pool_pages, T, H, D] (fp16 or bf16), checked
+    and packed once; the returned call enqueues it.
 
     Page i reads pool block ``block_table[i]`` (default i) and is written to out_blobs[i].  With
     ``neon_arith`` the groups are quantized with the reference's ARM NEON fp16 arithmetic (the bytes its
     ARM build writes) instead of its scalar x86-64 arithmetic.
+
+    The scalar arguments, ``base_sequence_nonce`` among them, are fixed when the call is prepared.  A
+    prepared egress that runs again over new data must therefore take fresh nonces through the
+    ``sequence_nonces`` tensor (read at every call): one nonce used twice under one key reuses ChaCha20
+    keystream.
     """
     dev = k_pool.device
     _require_cuda("k_pages", k_pool, (torch.float16, torch.bfloat16))
@@ -123,23 +169,36 @@ def encode_pages(k_pool: torch.Tensor, v_pool: torch.Tensor | None, token_hashes
                         tenant_id_hash, model_id_hash, layer_id, head_group_id,
                         capi.OPT_NEON_ARITH if neon_arith else 0, k_pool.shape[0])
     dtype = capi.DTYPE_BF16 if k_pool.dtype == torch.bfloat16 else capi.DTYPE_F16
-    rc = _on_device(dev, capi.load().ztcp_encode_pages, k_pool.data_ptr(), _ptr(v_pool), dtype, geom, batch,
-                    int(preset), int(rope_mode), int(expected_payload_bytes), keys, out_blobs.data_ptr(),
-                    _stream_handle(dev))
-    capi.check(rc)
+    args = (k_pool.data_ptr(), _ptr(v_pool), dtype, geom, batch, int(preset), int(rope_mode),
+            int(expected_payload_bytes), _copy_keys(keys), out_blobs.data_ptr())
+    keep = (k_pool, v_pool, token_hashes, out_blobs, block_table, sequence_nonces, layer_ids)
+    return PreparedCall(capi.load().ztcp_encode_pages, args, dev, keep)
+
+
+def _copy_keys(keys: capi.Keys) -> capi.Keys:
+    # a prepared call owns its key block: a caller that zeroizes or reuses its own after preparing changes
+    # nothing behind the call's back
+    return capi.Keys.from_buffer_copy(keys)
 
 
 def decode_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, out_k: torch.Tensor,
-                 out_v: torch.Tensor | None, *, rope_dim: int, is_mla: bool, tenant_id_hash: int,
-                 model_id_hash: int, layer_id: int, keys: capi.Keys, block_table: torch.Tensor | None = None,
-                 layer_ids: torch.Tensor | None = None, status: torch.Tensor | None = None,
-                 any_fail: torch.Tensor | None = None, check_block_table: bool = True,
-                 page_fallback: bool = False):
-    """Ingress of ``blobs.shape[0]`` pages into fp16 pools [pool_pages, T, H, D].
+                 out_v: torch.Tensor | None, *, stream=None, **kw):
+    """Ingress of ``blobs.shape[0]`` pages into fp16 pools [pool_pages, T, H, D], enqueued on `stream`
+    (default: the current stream); keyword arguments as for ``prepare_decode``.  Returns the device tensors
+    (status[n] int32, any_fail[1] int32)."""
+    return prepare_decode(blobs, token_hashes, out_k, out_v, **kw)(stream)
 
-    Enqueues verify + decrypt; returns the device tensors (status[n] int32, any_fail[1] int32).  When
-    any page fails, every output page of the batch is zeroed -- or, with ``page_fallback``, only the pages
-    whose status is non-zero (the others are decoded).
+
+def prepare_decode(blobs: torch.Tensor, token_hashes: torch.Tensor, out_k: torch.Tensor,
+                   out_v: torch.Tensor | None, *, rope_dim: int, is_mla: bool, tenant_id_hash: int,
+                   model_id_hash: int, layer_id: int, keys: capi.Keys, block_table: torch.Tensor | None = None,
+                   layer_ids: torch.Tensor | None = None, status: torch.Tensor | None = None,
+                   any_fail: torch.Tensor | None = None, check_block_table: bool = True,
+                   page_fallback: bool = False) -> PreparedCall:
+    """Ingress of ``blobs.shape[0]`` pages into fp16 pools [pool_pages, T, H, D], checked and packed once;
+    the returned call enqueues verify + decrypt and returns the device tensors (status[n] int32,
+    any_fail[1] int32), the same two at every call.  When any page fails, every output page of the batch is
+    zeroed -- or, with ``page_fallback``, only the pages whose status is non-zero (the others are decoded).
     """
     dev = blobs.device
     _require_cuda("cold_blobs", blobs, (torch.uint8,))
@@ -166,17 +225,18 @@ def decode_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, out_k: torch.T
     geom = capi.geometry(T, H, D, rope_dim, is_mla)
     batch = _page_batch(n, token_hashes, block_table, None, layer_ids, 0, tenant_id_hash, model_id_hash,
                         layer_id, 0, capi.OPT_PAGE_FALLBACK if page_fallback else 0, out_k.shape[0])
-    rc = _on_device(dev, capi.load().ztcp_decode_pages, blobs.data_ptr(), int(blob_bytes), geom, batch, keys,
-                    out_k.data_ptr(), _ptr(out_v), status.data_ptr(), any_fail.data_ptr(), _stream_handle(dev))
-    capi.check(rc)
-    return status, any_fail
+    args = (blobs.data_ptr(), int(blob_bytes), geom, batch, _copy_keys(keys), out_k.data_ptr(), _ptr(out_v),
+            status.data_ptr(), any_fail.data_ptr())
+    keep = (blobs, token_hashes, out_k, out_v, block_table, layer_ids)
+    return PreparedCall(capi.load().ztcp_decode_pages, args, dev, keep, (status, any_fail))
 
 
 def verify_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, *, num_tokens: int, num_heads: int,
                  head_dim: int, rope_dim: int, is_mla: bool, tenant_id_hash: int, model_id_hash: int, layer_id: int,
                  keys: capi.Keys, layer_ids: torch.Tensor | None = None, status: torch.Tensor | None = None,
-                 any_fail: torch.Tensor | None = None):
-    """Integrity check of stored blobs without decrypting; returns device (status[n], any_fail[1])."""
+                 any_fail: torch.Tensor | None = None, stream=None):
+    """Integrity check of stored blobs without decrypting, enqueued on `stream` (default: the current
+    stream); returns device (status[n], any_fail[1])."""
     dev = blobs.device
     _require_cuda("cold_blobs", blobs, (torch.uint8,))
     if blobs.dim() != 2:
@@ -190,7 +250,7 @@ def verify_pages(blobs: torch.Tensor, token_hashes: torch.Tensor, *, num_tokens:
     geom = capi.geometry(num_tokens, num_heads, head_dim, rope_dim, is_mla)
     batch = _page_batch(n, token_hashes, None, None, layer_ids, 0, tenant_id_hash, model_id_hash, layer_id, 0)
     rc = _on_device(dev, capi.load().ztcp_verify_pages, blobs.data_ptr(), int(blob_bytes), geom, batch, keys,
-                    status.data_ptr(), any_fail.data_ptr(), _stream_handle(dev))
+                    status.data_ptr(), any_fail.data_ptr(), _stream_arg(dev, stream))
     capi.check(rc)
     return status, any_fail
 
