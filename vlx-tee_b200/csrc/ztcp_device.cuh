@@ -521,6 +521,26 @@ __device__ __forceinline__ void dequant_int4(const uint32_t* q, uint16_t scale, 
     dequant_exact<4 * NQ>(q, 4, scale, out);
     return;
   }
+  if ((scale & 0x7C00u) >= 0x1400u) {
+    // scale / 16 is a normal fp16 (exponent field >= 5; subtracting 0x1000 lowers it by 4, exactly).  Output
+    // pair j (elements 2j, 2j + 1) comes from byte j copied into every byte: the low half keeps its low
+    // nibble (1024 + u), the high half its high nibble at bits 20-23 (1024 + 16u).  16 (u - 8) * (scale / 16)
+    // is then the same exact product as (u - 8) * scale, rounded once (every nibble and every such scale
+    // checked against the direct form on the CPU), with one permute and one mask per pair and no
+    // reordering of the results.
+    const __half2 s2 = bits_h2((uint32_t)scale | ((uint32_t)(scale - 0x1000u) << 16));
+    const __half2 bias = bits_h2(0x64806408u);  // (1032, 1152)
+#pragma unroll
+    for (int k = 0; k < NQ; ++k) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t p = (__byte_perm(q[k], 0u, 0x1111u * j) & 0x00F0000Fu) | 0x64006400u;
+        out[4 * k + j] = h2_bits(__hmul2_rn(__hsub2(bits_h2(p), bias), s2));
+      }
+    }
+    return;
+  }
+  // scales below 2^-10: the pairs (e0, e4) .. (e3, e7) at unit weight, reordered after the multiply
   const __half2 s2 = __half2half2(__ushort_as_half(scale));
   const __half2 bias = __float2half2_rn(1032.0f);  // 0x6400 | u = 1024 + u, q = u - 8
 #pragma unroll
