@@ -964,7 +964,7 @@ void launch_egress(const EgressParams& P, bool bf16, cudaStream_t stream) {
 void launch_mac(const MacParams& P, bool verify, cudaStream_t stream) {
   // A chain CTA is four warps, one per SM sub-partition, each running 32 independent per-page chains
   // that keep the sub-partition's ALU pipe busy.  The CTA takes the SM's whole shared memory (its
-  // lanes' input rings use 194 KB of it) so that no other CTA -- another chain CTA or a tile kernel
+  // lanes' input rings use 133 KB of it) so that no other CTA -- another chain CTA or a tile kernel
   // running concurrently on another stream -- is co-scheduled on its sub-partitions.
   static_assert(kRingBytes <= kMacReserveBytes, "chain rings must fit the reserved shared memory");
   const unsigned grid = (unsigned)((P.n_pages + kChainThreads - 1) / kChainThreads);
