@@ -719,7 +719,12 @@ def ours(args):
         eg = roof["egress_tile_kernel"]
         clk = clocks.summary()
         step_bytes = n * (PAGE_HOT_BYTES + BLOB_BYTES) * 2 * D    # read + write, egress + ingress, per GPU
-        alu_step_ms = 2 * n * D * (EXPECTED_PAYLOAD // 64) / peaks["chacha20_blocks_per_s"] * 1e3
+        # integer work of a step at the all-SM rates measured in this run: both directions' keystream blocks and
+        # both directions' tag-chain words (the two share the SMs' ALU pipes, so their times add); the
+        # quantizers' and dequantizers' integer work is left out, so the bound is a lower bound
+        chacha_step_ms = 2 * n * D * (EXPECTED_PAYLOAD // 64) / peaks["chacha20_blocks_per_s"] * 1e3
+        sip_step_ms = 2 * n * D * ((32 + EXPECTED_PAYLOAD) // 8 + 1) / peaks["sip_words_per_s"] * 1e3
+        alu_step_ms = chacha_step_ms + sip_step_ms
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K,
             "warmup": args.warmup, "ms_per_step": round(total_ms / K, 4), "higher_is_better": True,
@@ -755,12 +760,15 @@ def ours(args):
                 "bytes_per_step": step_bytes,
                 "hbm_bound_ms": round(step_bytes / (peak * 1e9) * 1e3, 4),
                 "alu_bound_ms": round(alu_step_ms, 4),
+                "alu_chacha20_ms": round(chacha_step_ms, 4),
+                "alu_siphash_ms": round(sip_step_ms, 4),
                 "chain_sm_ms_per_step": round(D * -(-n // 128) * (kt["mac_kernel<sign>"] + kt["mac_kernel<verify>"]), 3),
                 "achieved_ms_per_step": round(total_ms / K, 4),
                 "frac": round(max(step_bytes / (peak * 1e9) * 1e3, alu_step_ms) / (total_ms / K), 4),
-                "note": "per GPU and step: HBM bytes of both tile kernels and both chains at the measured copy "
-                        "bandwidth, ChaCha20 keystream of both directions at the block rate measured in this run; "
-                        "chain_sm_ms_per_step = SM-milliseconds the SM-exclusive tag chains hold per step"},
+                "note": "per GPU and step: hot K/V and blob bytes of both directions (each read or written once) at "
+                        "the measured copy bandwidth; ALU = ChaCha20 blocks and SipHash words of both directions at "
+                        "the all-SM rates measured in this run (quantizer work not counted); frac = max(HBM, ALU) / "
+                        "achieved; chain_sm_ms_per_step = SM-milliseconds the SM-exclusive tag chains hold per step"},
             "clocks": clk,
             "host": {"enqueue_ms_max_over_ranks": round(host_enqueue_max, 3), "enqueue_ms_rank0": round(host_enqueue_ms, 3),
                      "wall_ms_max_over_ranks": round(wall_max, 3), "gpu_ms_max_over_ranks": round(total_ms, 3),
