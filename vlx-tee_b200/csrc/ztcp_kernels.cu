@@ -140,14 +140,23 @@ __device__ __forceinline__ void split_item(int it, const SectionTile& t, int& ve
   }
 }
 
-template <int KIND, bool BF16, bool NEON>
+// STAGED: the tile's rows are in shared memory (t.src points there); otherwise they are read from the KV
+// pool through the read-only data path.
+template <int KIND, bool BF16, bool NEON, bool STAGED = false>
 __device__ __forceinline__ void quantize_section(const SectionTile& t, const PackMul& mu) {
   const int items = t.tv * t.groups;
   for (int it = threadIdx.x; it < items; it += blockDim.x) {
     int vec, g;
     split_item(it, t, vec, g);
-    uint32_t w[8];
-    load_group16<false>(t.src + vec * t.row_stride + g * 16, w);  // raw bits
+    uint32_t w[8];  // raw bits
+    if (STAGED) {
+      const uint4* p = reinterpret_cast<const uint4*>(t.src + vec * t.row_stride + g * 16);
+      const uint4 a = p[0], b = p[1];
+      w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+      w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+    } else {
+      load_group16<false>(t.src + vec * t.row_stride + g * 16, w);
+    }
     uint8_t* qd = t.q + vec * t.q_bpv;
     if (KIND == kRaw) {
       if (BF16) {
@@ -229,15 +238,50 @@ __constant__ constexpr StaticEgress kStaticEgress[kStaticEgressCount] = {
 __constant__ constexpr StaticIngress kStaticIngress[kStaticIngressCount] = {
     make_static_ingress(kStaticIngressGeometry[0]), make_static_ingress(kStaticIngressGeometry[1])};
 
+// The 32-byte header of a page (csrc:61-75, :1129-1140).
+__device__ __forceinline__ void write_header(uint8_t* blob, int32_t flags, const PageMeta& m, int64_t page, uint64_t seq,
+                                             uint16_t layer) {
+  const uint64_t tok = m.token_hash[page];
+  const uint32_t hw[8] = {(uint32_t)kMagic | ((uint32_t)kVersion << 16) | ((uint32_t)flags << 24),
+                          m.tenant,
+                          m.model,
+                          (uint32_t)layer | ((uint32_t)m.head_group << 16),
+                          (uint32_t)tok,
+                          (uint32_t)(tok >> 32),
+                          (uint32_t)seq,
+                          (uint32_t)(seq >> 32)};
+  if ((reinterpret_cast<uintptr_t>(blob) & 3) == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) reinterpret_cast<uint32_t*>(blob)[i] = hw[i];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) blob[i] = (uint8_t)(hw[i >> 2] >> (8 * (i & 3)));
+  }
+}
+
+// Waits for phase 0 of a shared-memory mbarrier, at most 2^20 suspending tries; true when the phase completed.
+__device__ __forceinline__ bool mbar_wait_parity0(uint32_t bar) {
+  for (int it = 0; it < (1 << 20); ++it) {
+    uint32_t done;
+    asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0; selp.u32 %0, 1, 0, p; }"
+                 : "=r"(done)
+                 : "r"(bar)
+                 : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
 // ------------------------------------------------------------------------------------------------
 // Egress: quantize + pack + encrypt one (page, vec-tile)
 // ------------------------------------------------------------------------------------------------
-// 7 resident CTAs per SM (the register cap this implies was measured ~5 % faster than 6).
+// 7 resident CTAs per SM (the register cap this implies was measured ~5 % faster than 6), 5 for the compiled
+// geometries that stage their rows (egress_min_blocks).
 // CFG = 0: layout, tiling and staging plan from the launch parameters; CFG = i > 0: those of kStaticEgress[i - 1]
 // as compile-time constants (a whole-batch launch of that geometry and format), so their address and index
 // arithmetic folds away.
 template <bool BF16, bool NEON, int CFG>
-__global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __grid_constant__ EgressParams P) {
+__global__ void __launch_bounds__(kTileThreads, egress_min_blocks(CFG)) egress_tile_kernel(const __grid_constant__ EgressParams P) {
   extern __shared__ __align__(16) uint8_t stage[];
   __shared__ RangeTable T;
   const StaticEgress& G = kStaticEgress[CFG > 0 ? CFG - 1 : 0];
@@ -275,6 +319,85 @@ __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __gr
   const uint16_t* kp = P.k + blk * page_elems;
   const uint16_t* vp = P.v ? P.v + blk * page_elems : nullptr;
 
+  if (CFG && G.rows_ok && planned) {
+    // Staged rows: one thread starts two bulk copies of the tile's K and V rows into shared memory, completing
+    // on an mbarrier, and every thread computes its keystream block while they land -- the load latency that
+    // the quantizer would otherwise wait out hides under the keystream.
+    __shared__ __align__(8) uint64_t rows_bar;
+    uint8_t* kin = stage + G.stage_bytes;
+    uint8_t* vin = kin + G.rows_bytes;
+    const uint32_t bar = (uint32_t)__cvta_generic_to_shared(&rows_bar);
+    if (threadIdx.x == 0) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(bar) : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar),
+                   "r"((uint32_t)(vp ? 2 * G.rows_bytes : G.rows_bytes))
+                   : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       (uint32_t)__cvta_generic_to_shared(kin)),
+                   "l"(kp + v0 * head_dim), "r"((uint32_t)G.rows_bytes), "r"(bar)
+                   : "memory");
+      if (vp)
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         (uint32_t)__cvta_generic_to_shared(vin)),
+                     "l"(vp + v0 * head_dim), "r"((uint32_t)G.rows_bytes), "r"(bar)
+                     : "memory");
+    }
+    const uint64_t seq = page_seq(P.meta, page);
+    const uint16_t layer = page_layer(P.meta, page);
+    const uint32_t n2 = ((uint32_t)layer << 16) | P.meta.head_group;
+    const int bi = threadIdx.x;  // this thread's block of the tile (one per thread: rows_ok)
+    const bool has_block = bi < plan.first[plan.n];
+    uint32_t ks[16];
+    int kb = 0, soff = 0;
+    if (has_block) {
+      const int i = plan_range(plan, bi);
+      const int rel = bi - plan.first[i];
+      kb = plan.kb0[i] + tile * (plan.first[i + 1] - plan.first[i]) + rel;
+      soff = plan.stage[i] + rel * 64;
+      chacha20_block(P.key, (uint32_t)(1 + kb), (uint32_t)seq, (uint32_t)(seq >> 32), n2, ks);
+    }
+    __syncthreads();  // the barrier's initialization is visible to every thread
+    // Bounded wait: each try_wait suspends for a while, and the copies read valid pool memory, so they land
+    // within microseconds.  Should they not within the limit, the threads copy the rows themselves -- the
+    // same bytes the bulk copies carry, so a copy landing late changes nothing -- and thread 0 waits once
+    // more, with the same limit, before the CTA gives up its shared memory.
+    const bool landed = __syncthreads_and(mbar_wait_parity0(bar));
+    if (!landed) {
+      const uint4* ks16 = reinterpret_cast<const uint4*>(kp + v0 * head_dim);
+      const uint4* vs16 = vp ? reinterpret_cast<const uint4*>(vp + v0 * head_dim) : nullptr;
+      for (int c = threadIdx.x; c < G.rows_bytes / 16; c += kTileThreads) {
+        reinterpret_cast<uint4*>(kin)[c] = __ldg(ks16 + c);
+        if (vs16) reinterpret_cast<uint4*>(vin)[c] = __ldg(vs16 + c);
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int s = 0; s < 3; ++s) {
+      if (s >= L.n) break;
+      const Section S = L.sec[s];
+      const SectionTile st{reinterpret_cast<const uint16_t*>(S.buf ? vin : kin) + S.col, stage + stage_q[s],
+                           stage + stage_s[s], head_dim, S.q_bpv, S.s_bpv, S.dim >> 4, gshift[s], tv};
+      if (S.kind == kInt4) quantize_section<kInt4, BF16, NEON, true>(st, P.mul);
+      else if (S.kind == kInt8) quantize_section<kInt8, BF16, NEON, true>(st, P.mul);
+      else quantize_section<kRaw, BF16, NEON, true>(st, P.mul);
+    }
+    if (tile == 0 && threadIdx.x == 0) write_header(blob, G.flags, P.meta, page, seq, layer);
+    __syncthreads();
+    if (has_block) {
+      const uint4* src = reinterpret_cast<const uint4*>(stage + soff);
+      uint4* dst = reinterpret_cast<uint4*>(blob + kHeaderBytes + (int64_t)kb * 64);
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        uint4 pt = src[w];
+        pt.x ^= ks[4 * w]; pt.y ^= ks[4 * w + 1]; pt.z ^= ks[4 * w + 2]; pt.w ^= ks[4 * w + 3];
+        dst[w] = pt;
+      }
+    }
+    if (!landed && threadIdx.x == 0) mbar_wait_parity0(bar);
+    return;
+  }
+
   // ---- phase 1: quantize this tile's rows of every section this launch produces into shared memory
 #pragma unroll
   for (int s = 0; s < 3; ++s) {
@@ -291,24 +414,8 @@ __global__ void __launch_bounds__(kTileThreads, 7) egress_tile_kernel(const __gr
   // header (32 bytes) by tile 0 (a wire-order egress leaves it to its last tag segment)
   const uint64_t seq = page_seq(P.meta, page);
   const uint16_t layer = page_layer(P.meta, page);
-  if (tile == 0 && threadIdx.x == 0 && (CFG || P.write_header)) {
-    const uint64_t tok = P.meta.token_hash[page];
-    const uint32_t hw[8] = {(uint32_t)kMagic | ((uint32_t)kVersion << 16) | ((uint32_t)(CFG ? G.flags : P.flags) << 24),
-                            P.meta.tenant,
-                            P.meta.model,
-                            (uint32_t)layer | ((uint32_t)P.meta.head_group << 16),
-                            (uint32_t)tok,
-                            (uint32_t)(tok >> 32),
-                            (uint32_t)seq,
-                            (uint32_t)(seq >> 32)};
-    if ((reinterpret_cast<uintptr_t>(blob) & 3) == 0) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) reinterpret_cast<uint32_t*>(blob)[i] = hw[i];
-    } else {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) blob[i] = (uint8_t)(hw[i >> 2] >> (8 * (i & 3)));
-    }
-  }
+  if (tile == 0 && threadIdx.x == 0 && (CFG || P.write_header))
+    write_header(blob, CFG ? G.flags : P.flags, P.meta, page, seq, layer);
   __syncthreads();
 
   // ---- phase 2: encrypt this tile's byte ranges
@@ -907,8 +1014,10 @@ bool same3(const int32_t (&a)[3], const int32_t (&b)[3]) { return a[0] == b[0] &
 template <bool BF16, bool NEON, int CFG>
 void launch_egress_t(const EgressParams& P, cudaStream_t stream) {
   const int64_t grid = P.n_pages * P.tiles;
-  ensure_smem(egress_tile_kernel<BF16, NEON, CFG>, P.stage_bytes);
-  egress_tile_kernel<BF16, NEON, CFG><<<(unsigned)grid, kTileThreads, P.stage_bytes, stream>>>(P);
+  // a compiled geometry that stages its rows takes their room after the staging area
+  const int32_t smem = CFG ? kStaticEgressHost[CFG - 1].rows_smem : P.stage_bytes;
+  ensure_smem(egress_tile_kernel<BF16, NEON, CFG>, smem);
+  egress_tile_kernel<BF16, NEON, CFG><<<(unsigned)grid, kTileThreads, smem, stream>>>(P);
 }
 
 template <bool BF16>

@@ -214,6 +214,10 @@ struct StaticEgress {
   int32_t stage_q[3] = {}, stage_s[3] = {}, gshift[3] = {};
   int32_t tile_vecs = 0, n_tiles = 0, head_dim = 0, flags = 0, stage_bytes = 0;
   int64_t vecs = 0, page_elems = 0;
+  // Staged rows: a full tile's K and V rows (tile_vecs x head_dim each, contiguous in the pool) are copied to
+  // shared memory after the staging area by two bulk copies while every thread computes its keystream block
+  // (one block per thread: the plan's blocks fit the CTA).  rows_smem = the launch's dynamic shared memory.
+  int32_t rows_ok = 0, rows_bytes = 0, rows_smem = 0;
 };
 
 ZTCP_HD StaticEgress make_static_egress(int preset, int rope_mode, StaticGeometry g) {
@@ -228,14 +232,28 @@ ZTCP_HD StaticEgress make_static_egress(int preset, int rope_mode, StaticGeometr
   e.stage_bytes = plan_stage(e.L, e.tile_vecs, e.stage_q, e.stage_s);
   build_tile_plan(e.L, e.tile_vecs, e.stage_q, e.stage_s, true, &e.plan);
   for (int i = 0; i < 3; ++i) e.gshift[i] = i < e.L.n ? log2_or_minus1(e.L.sec[i].dim / kGroup) : -1;
+  e.rows_bytes = e.tile_vecs * g.head_dim * 2;
+  e.rows_ok = e.plan.ok && e.plan.first[e.plan.n] <= kTileThreads && e.stage_bytes % 16 == 0 && e.rows_bytes % 16 == 0 &&
+              e.stage_bytes + (g.has_v ? 2 : 1) * e.rows_bytes <= 48 * 1024;
+  e.rows_smem = e.rows_ok ? e.stage_bytes + (g.has_v ? 2 : 1) * e.rows_bytes : e.stage_bytes;
   return e;
 }
+
 
 // (preset, rope_mode) and geometry of each compiled egress: INT4_SYM and K8V4_ASYM with PRESERVE_FP8 on GQA
 // pages, INT4_SYM with PRESERVE_FP8 on MLA pages.
 constexpr int kStaticEgressCount = 3;
 constexpr int kStaticEgressKeys[kStaticEgressCount][2] = {{1, 1}, {2, 1}, {1, 1}};
 constexpr StaticGeometry kStaticEgressGeometry[kStaticEgressCount] = {kGqa64x8x128, kGqa64x8x128, kMla64x1x576};
+
+// Resident CTAs per SM the compiled egress kernel is built for: 5 with staged rows (45-47 KB of shared memory
+// and up to 48 registers per thread), 7 otherwise.
+ZTCP_HD int egress_min_blocks(int cfg) {
+  return cfg > 0 && make_static_egress(kStaticEgressKeys[cfg - 1][0], kStaticEgressKeys[cfg - 1][1],
+                                       kStaticEgressGeometry[cfg - 1]).rows_ok
+             ? 5
+             : 7;
+}
 
 // Ingress: a geometry with the layouts of every flags byte a header may carry, two of them (the benchmark
 // formats) compiled into their own copies of the tile code.
