@@ -191,3 +191,59 @@ def test_config4_prefix_4096_pages_bit_exact(oracle, preset, payload):
     for a, bad_blob, bad_dec in _oracle_chunks(check_layer, P, 64):   # one chunk = one layer's 64 pages
         assert not bad_blob, f"blobs of layer {a // 64} differ from the oracle"
         assert not bad_dec, f"decoded pages of layer {a // 64} differ from the oracle"
+
+
+@pytest.mark.parametrize("shape_name,preset", [("GQA", 1), ("GQA", 2), ("MLA", 1)])
+def test_compiled_geometries_with_and_without_padding(oracle, shape_name, preset):
+    """The compiled tile kernels (the benchmark geometries and formats) on their every path: whole tiles
+    (the GQA egress stages its rows in shared memory by bulk copies), and a padded payload, whose last tile
+    takes the general path inside the same kernel; fp16 and bf16 input with edge values, every byte against
+    the oracle."""
+    import ctypes as C
+
+    from ztcp_b200 import capi, codec, workload
+
+    shape = getattr(workload, shape_name)
+    g = capi.geometry(shape.num_tokens, shape.num_heads, shape.head_dim, shape.rope_dim, shape.mla)
+    base = capi.load().ztcp_spec_payload_bytes(preset, 1, C.byref(g), 0 if shape.mla else 1)
+    rng = np.random.default_rng(606 + preset)
+    edge = np.array([np.inf, -np.inf, 65504, -65504, 1e-7, -3e-6, 0.0, 7e4], dtype=np.float32)
+    pages = 6
+    for extra in (0, 16, 64):
+        for bf16 in (False, True):
+            k32, v32 = workload.kv_pages_np(pages, shape, seed=int(rng.integers(1 << 30)))
+            for a in (k32, v32):
+                if a is not None:
+                    mask = rng.random(a.shape) < 0.01
+                    a[mask] = rng.choice(edge, int(mask.sum()))
+            with np.errstate(over="ignore"):
+                if bf16:
+                    kt = torch.from_numpy(k32).to(torch.bfloat16)
+                    vt = None if v32 is None else torch.from_numpy(v32).to(torch.bfloat16)
+                    k16, v16 = kt.half().numpy(), None if vt is None else vt.half().numpy()
+                else:
+                    k16, v16 = k32.astype(np.float16), None if v32 is None else v32.astype(np.float16)
+                    kt, vt = torch.from_numpy(k16), None if v16 is None else torch.from_numpy(v16)
+            m = workload.session_material(int(rng.integers(1 << 30)))
+            toks = workload.token_hashes(pages, int(rng.integers(1 << 30)))
+            exp = base + extra
+            keys = capi.keys(*m["key"], *m["mac_key"])
+            blobs = torch.empty((pages, 48 + exp), dtype=torch.uint8, device=DEV)
+            codec.encode_pages(kt.to(DEV), None if vt is None else vt.to(DEV), torch.from_numpy(toks).to(DEV), blobs,
+                               rope_dim=shape.rope_dim, preset=preset, rope_mode=1, expected_payload_bytes=exp,
+                               tenant_id_hash=m["tenant"], model_id_hash=m["model"], layer_id=m["layer"],
+                               head_group_id=m["head_group"], base_sequence_nonce=m["base_seq"], keys=keys)
+            want = helpers.oracle_encode(oracle, k16, v16, toks, shape.rope_dim, preset, 1, exp, m)
+            tag = f"{shape_name} preset {preset} +{extra} bf16 {bf16}"
+            np.testing.assert_array_equal(blobs.cpu().numpy(), want, err_msg=tag)
+            kd = torch.empty(tuple(k16.shape), dtype=torch.float16, device=DEV)
+            vd = None if v16 is None else torch.empty_like(kd)
+            st, fail = codec.decode_pages(blobs, torch.from_numpy(toks).to(DEV), kd, vd, rope_dim=shape.rope_dim,
+                                          is_mla=shape.mla, tenant_id_hash=m["tenant"], model_id_hash=m["model"],
+                                          layer_id=m["layer"], keys=keys)
+            codec.raise_for_status(st, fail)
+            okd, ovd, _, first = helpers.oracle_decode(oracle, want, toks, k16.shape, shape.rope_dim, shape.mla, m)
+            assert first == -1, tag
+            np.testing.assert_array_equal(kd.cpu().numpy().view(np.uint16), okd, err_msg=tag)
+            if vd is not None:
+                np.testing.assert_array_equal(vd.cpu().numpy().view(np.uint16), ovd, err_msg=tag)
