@@ -259,17 +259,19 @@ __device__ __forceinline__ void write_header(uint8_t* blob, int32_t flags, const
   }
 }
 
-// Waits for phase 0 of a shared-memory mbarrier, at most 2^20 suspending tries; true when the phase completed.
+// Waits for phase 0 of a shared-memory mbarrier for at most 2^31 SM clock cycles (about a second at the
+// B200's 1.97 GHz; each try_wait may suspend the thread for a while); true when the phase completed.
 __device__ __forceinline__ bool mbar_wait_parity0(uint32_t bar) {
-  for (int it = 0; it < (1 << 20); ++it) {
+  const long long t0 = clock64();
+  for (;;) {
     uint32_t done;
     asm volatile("{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], 0; selp.u32 %0, 1, 0, p; }"
                  : "=r"(done)
                  : "r"(bar)
                  : "memory");
     if (done) return true;
+    if (clock64() - t0 > (1ll << 31)) return false;
   }
-  return false;
 }
 
 // ------------------------------------------------------------------------------------------------
